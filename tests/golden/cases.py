@@ -1,0 +1,141 @@
+"""Definitions of the golden-vector cases (inputs are rebuilt from seeds).
+
+Used by ``make_golden.py`` (which runs the reference implementation on them)
+and by the tests (which rebuild the same inputs and compare with the stored
+outputs).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import inputs as gi
+
+f32 = np.float32
+
+RATIOS = [0.8, 0.85, 0.9, 0.95, 1.0]
+
+
+def rtn_weight(case: dict) -> np.ndarray:
+    M, N, seed = case["M"], case["N"], case["seed"]
+    if case.get("dist") == "heavy":
+        W = gi.weight_heavy_tail(seed, M, N)
+    else:
+        W = gi.weight_outlier_cols(seed, M, N, frac=case.get("frac", 0.004))
+    # edge rows: all-zero row, constant row, single spike, all-positive, all-negative
+    if M >= 8:
+        W[1] = 0.0
+        W[2] = 0.01
+        W[3] = 0.0
+        W[3, N // 3] = 0.5
+        W[4] = np.abs(W[4]) + 0.05
+        W[5] = -np.abs(W[5]) - 0.05
+    return W
+
+
+RTN_CASES = {
+    "rtn4_sym_r256": dict(M=64, N=1024, seed=11, rot=256, bits=4, asym=False, ratios=None, gs=None),
+    "rtn4_sym_r256_clip": dict(M=64, N=1024, seed=12, rot=256, bits=4, asym=False, ratios=RATIOS, gs=None),
+    "rtn4_sym_r64_pad": dict(M=48, N=200, seed=13, rot=64, bits=4, asym=False, ratios=None, gs=None),
+    "rtn4_sym_g128": dict(M=32, N=512, seed=14, rot=16, bits=4, asym=False, ratios=None, gs=128),
+    "rtn4_sym_g96_clip": dict(M=32, N=500, seed=15, rot=0, bits=4, asym=False, ratios=RATIOS, gs=96),
+    "rtn4_asym_r256": dict(M=64, N=768, seed=16, rot=256, bits=4, asym=True, ratios=None, gs=None),
+    "rtn4_asym_r256_clip": dict(M=64, N=768, seed=17, rot=256, bits=4, asym=True, ratios=RATIOS, gs=None),
+    "rtn4_asym_g64": dict(M=32, N=256, seed=18, rot=0, bits=4, asym=True, ratios=None, gs=64),
+    "rtn8_sym_r64": dict(M=64, N=768, seed=19, rot=64, bits=8, asym=False, ratios=None, gs=None, dist="heavy"),
+    "rtn8_sym_r64_clip": dict(M=96, N=768, seed=20, rot=64, bits=8, asym=False, ratios=RATIOS, gs=None, dist="heavy"),
+    "rtn8_asym_r16": dict(M=64, N=384, seed=21, rot=16, bits=8, asym=True, ratios=None, gs=None),
+    "rtn8_asym_r64_clip": dict(M=64, N=384, seed=22, rot=64, bits=8, asym=True, ratios=RATIOS, gs=None, dist="heavy"),
+}
+
+ROT_CASES = {
+    "rotw_r16": dict(M=16, N=128, seed=31, rot=16),
+    "rotw_r64_pad": dict(M=24, N=300, seed=32, rot=64),
+    "rotw_r256": dict(M=16, N=512, seed=33, rot=256),
+    "rotw_r32_sylvester": dict(M=8, N=96, seed=34, rot=32),
+}
+
+ROTH_CASES = {
+    "roth_r64_pad": dict(N=200, rot=64, seed=41, nblk=None),
+    "roth_r256": dict(N=512, rot=256, seed=42, nblk=None),
+    "roth_3d_r64": dict(N=128, rot=64, seed=43, nblk=3),
+}
+
+GPTQ_CASES = {
+    # single block: the column loop alone (bit-exact given the same Hinv)
+    "gptq4_single_block": dict(M=8, N=32, seed=51, bits=4, asym=False, bs=32, nsamp=64, rot=0),
+    "gptq4_r256": dict(M=64, N=512, seed=52, bits=4, asym=False, bs=128, nsamp=1024, rot=256),
+    "gptq4_r64_ragged_block": dict(M=40, N=320, seed=53, bits=4, asym=False, bs=128, nsamp=512, rot=64),
+    "gptq8_sym": dict(M=48, N=256, seed=54, bits=8, asym=False, bs=128, nsamp=512, rot=256),
+    "gptq8_asym": dict(M=48, N=256, seed=55, bits=8, asym=True, bs=64, nsamp=512, rot=256),
+    "gptq4_blockdiag": dict(M=32, N=256, seed=56, bits=4, asym=False, bs=64, nsamp=512, rot=0, nblk=2),
+    "gptq4_rank_deficient": dict(M=32, N=384, seed=57, bits=4, asym=False, bs=128, nsamp=128, rot=256),
+}
+
+LDLQ_CASES = {
+    "ldlq4_weight_only": dict(M=64, N=256, seed=61, bits=4, iters=1, greedy=0, bs=128, rot=256),
+    "ldlq4_iter2_greedy2": dict(M=48, N=256, seed=62, bits=4, iters=2, greedy=2, bs=64, rot=256),
+    "ldlq8_calib": dict(M=32, N=256, seed=63, bits=8, iters=1, greedy=0, bs=128, rot=0, calib=True),
+}
+
+GREEDY_CASES = {
+    "greedy4": dict(M=32, N=128, seed=71, bits=4, passes=2),
+    "greedy8": dict(M=16, N=64, seed=72, bits=8, passes=1),
+}
+
+PISO_CASES = {
+    "piso_int8_sym": dict(M=32, N=512, seed=81, kind="int8"),
+    "piso_int8_asym": dict(M=32, N=512, seed=82, kind="int8_asym"),
+    "piso_int4_sym": dict(M=32, N=512, seed=83, kind="int4"),
+    "piso_int4_asym": dict(M=32, N=512, seed=84, kind="int4_asym"),
+}
+
+PACK_CASES = {
+    "pack_even": dict(M=16, K=64, seed=91),
+    "pack_odd": dict(M=7, K=33, seed=92),
+}
+
+LINSPACE_CASES = {
+    "ls_coarse_sym": (0.5, 2.0, 128),
+    "ls_coarse_asym8": (0.8, 1.2, 128),
+    "ls_fine": (0.95, 1.05, 16),
+    "ls_small": (0.5, 2.0, 7),
+}
+
+
+def gptq_inputs(case: dict):
+    M, N, seed = case["M"], case["N"], case["seed"]
+    W = gi.weight_outlier_cols(seed, M, N)
+    H = gi.hessian_lognormal(seed + 1000, N, case["nsamp"])
+    if case.get("nblk"):
+        nb = case["nblk"]
+        bs = N // nb
+        H = np.stack([H[i * bs:(i + 1) * bs, i * bs:(i + 1) * bs] for i in range(nb)])
+    return W, H
+
+
+def ldlq_inputs(case: dict):
+    M, N, seed = case["M"], case["N"], case["seed"]
+    W = gi.weight_outlier_cols(seed, M, N, frac=0.01, mult=30.0, std=0.015)
+    H = gi.hessian_lognormal(seed + 1000, N, 512) if case.get("calib") else None
+    return W, H
+
+
+def greedy_inputs(case: dict):
+    M, N, seed = case["M"], case["N"], case["seed"]
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((M, N)) * 0.02).astype(f32)
+    qmax = 7 if case["bits"] == 4 else 127
+    s = (np.abs(W).max(axis=1, keepdims=True) / qmax).astype(f32)
+    Q = np.clip(np.rint(W / s), -qmax - 1, qmax).astype(np.int8)
+    H = gi.hessian_lognormal(seed + 1000, N, 256)
+    H = (H + 0.01 * np.mean(np.diag(H)) * np.eye(N)).astype(f32)
+    return W, Q, np.broadcast_to(s, (M, N)).astype(f32).copy(), H
+
+
+def piso_inputs(case: dict):
+    M, N, seed = case["M"], case["N"], case["seed"]
+    W = gi.weight_outlier_cols(seed, M, N)
+    rng = np.random.default_rng(seed + 7)
+    hd = rng.lognormal(0.0, 1.0, size=N).astype(f32) ** 2
+    return W, hd.astype(f32)

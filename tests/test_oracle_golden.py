@@ -1,0 +1,138 @@
+"""The CPU oracle (oracle/cpu_ref.py) against golden vectors made by the reference.
+
+These pin the oracle before it is trusted as the checker of the CUDA path.
+Tolerances are the parity bar of the task: codes/packed bytes bit-exact,
+scales exact; GPTQ/LDLQ through tr(E H E^T) (GPTQ-hinv is chaotic, so codes of
+the larger cases differ in a few positions between any two fp32 inverses).
+"""
+
+import numpy as np
+import pytest
+
+from oracle import cpu_ref as R
+from tests.golden import cases as C
+from tests.golden import inputs as gi
+
+
+def test_hadamard_and_rounding(golden):
+    for n in (16, 64, 256):
+        assert np.array_equal(R.make_hadamard_regular(n), golden[f"hadamard_{n}/H"])
+    assert np.array_equal(R.rhaz(golden["kat_rhaz/x"]), golden["kat_rhaz/y"])
+    for k, (a, b, n) in C.LINSPACE_CASES.items():
+        assert np.array_equal(R.torch_linspace_f32(a, b, n), golden[k + "/v"])
+
+
+@pytest.mark.parametrize("name", list(C.ROT_CASES))
+def test_rotate_weights(golden, name):
+    c = C.ROT_CASES[name]
+    W = gi.weight_outlier_cols(c["seed"], c["M"], c["N"])
+    assert gi.checksum(W) == str(golden[name + "/chk"])
+    g = golden[name + "/Wrot"]
+    np.testing.assert_allclose(R.rotate_weights(W, c["rot"]), g, rtol=0, atol=1e-6 * np.abs(g).max())
+
+
+@pytest.mark.parametrize("name", list(C.ROTH_CASES))
+def test_rotate_hessian(golden, name):
+    c = C.ROTH_CASES[name]
+    H = gi.hessian_lognormal(c["seed"], c["N"], 256)
+    if c["nblk"]:
+        H = np.stack([H] * c["nblk"]) * np.arange(1, c["nblk"] + 1, dtype=np.float32)[:, None, None]
+    g = golden[name + "/Hrot"]
+    np.testing.assert_allclose(R.rotate_hessian(H, c["rot"]), g, rtol=0, atol=1e-6 * np.abs(g).max())
+
+
+def rtn_oracle(c):
+    W = C.rtn_weight(c)
+    Ww = R.rotate_weights(W, c["rot"]) if c["rot"] else W
+    gs = c["gs"] or Ww.shape[1]
+    if c["bits"] == 4 and not c["asym"]:
+        s = R.calculate_scales(Ww, gs, c["ratios"])
+        return Ww, s, None, R.quantize_weights(Ww, s, gs)
+    if c["bits"] == 4:
+        s, zp = R.calculate_scales_asymmetric(Ww, gs, c["ratios"])
+        return Ww, s, zp, R.quantize_weights_asymmetric(Ww, s, zp, gs)
+    if not c["asym"]:
+        s = R.calculate_scales_int8(Ww, c["ratios"])
+        return Ww, s, None, R.quantize_weights_int8(Ww, s)
+    s, zp = R.calculate_scales_int8_asymmetric(Ww, c["ratios"])
+    return Ww, s, zp, R.quantize_weights_int8_asymmetric(Ww, s, zp)
+
+
+@pytest.mark.parametrize("name", list(C.RTN_CASES))
+def test_rtn(golden, name):
+    c = C.RTN_CASES[name]
+    _, s, zp, q = rtn_oracle(c)
+    assert np.array_equal(s, golden[name + "/scales"])
+    assert np.array_equal(q, golden[name + "/codes"])
+    if zp is not None:
+        assert np.array_equal(zp, golden[name + "/zp"])
+    if c["bits"] == 4:
+        assert np.array_equal(R.pack_int4(q), golden[name + "/packed"])
+
+
+@pytest.mark.parametrize("name", list(C.PACK_CASES))
+def test_pack(golden, name):
+    c = C.PACK_CASES[name]
+    q = gi.codes(c["seed"], c["M"], c["K"])
+    p = R.pack_int4(q)
+    assert np.array_equal(p, golden[name + "/packed"])
+    assert np.array_equal(R.unpack_int4(p, c["K"]), q)
+    with pytest.raises(R.INT4PackingError):
+        R.pack_int4(np.array([[8, 0]], np.int8))
+
+
+@pytest.mark.parametrize("name", list(C.GPTQ_CASES))
+def test_gptq(golden, name):
+    c = C.GPTQ_CASES[name]
+    W, H = C.gptq_inputs(c)
+    Ww = R.rotate_weights(W, c["rot"]) if c["rot"] else W
+    Hr = R.rotate_hessian(H, c["rot"]) if c["rot"] else H
+    r = R.gptq_quantize_layer(Ww, Hr, c["bs"], 0.01, c["bits"], c["asym"])
+    assert np.array_equal(r["scales"], golden[name + "/scales"])
+    if r["zero_points"] is not None:
+        assert np.array_equal(r["zero_points"], golden[name + "/zp"])
+    assert np.mean(r["quantized_W"] == golden[name + "/codes"]) > 0.99
+    if Hr.ndim == 2:
+        p = R.proxy_loss(Ww, r["quantized_W"], r["scales"].astype(np.float32), r["zero_points"], Hr)
+        assert abs(p / float(golden[name + "/proxy"]) - 1) < 0.01
+    if name + "/Hinv" in golden:  # the column loop alone is bit-exact given the same Hinv
+        s, zp = R.gptq_row_params(Ww, c["bits"], c["asym"])
+        Q = np.zeros(Ww.shape, np.int8)
+        R.gptq_block(Ww.copy(), Q, s, golden[name + "/Hinv"], 0, Ww.shape[1], c["bs"], -8, 7, zp)
+        assert np.array_equal(Q, golden[name + "/codes"])
+
+
+@pytest.mark.parametrize("name", list(C.LDLQ_CASES))
+def test_ldlq(golden, name):
+    c = C.LDLQ_CASES[name]
+    W, H = C.ldlq_inputs(c)
+    Ww = R.rotate_weights(W, c["rot"]) if c["rot"] else W
+    Hr = None if H is None else (R.rotate_hessian(H, c["rot"]) if c["rot"] else H)
+    r = R.ldlq_quantize_layer(Ww, Hr, c["bs"], 0.01, c["bits"], c["iters"], c["greedy"])
+    Hp = Hr if Hr is not None else Ww.astype(np.float64).T @ Ww.astype(np.float64) / Ww.shape[0]
+    p = R.proxy_loss(Ww, r["quantized_W"], r["scales"].astype(np.float32), None, Hp)
+    assert abs(p / float(golden[name + "/proxy"]) - 1) < 0.005
+    assert np.mean(r["quantized_W"] == golden[name + "/codes"]) > 0.99
+
+
+@pytest.mark.parametrize("name", list(C.GREEDY_CASES))
+def test_greedy(golden, name):
+    c = C.GREEDY_CASES[name]
+    W, Q, S, H = C.greedy_inputs(c)
+    qm = (-8, 7) if c["bits"] == 4 else (-128, 127)
+    assert np.array_equal(R.greedy_local_search(W, Q, S, H, c["passes"], *qm), golden[name + "/codes"])
+
+
+@pytest.mark.parametrize("name", list(C.PISO_CASES))
+def test_piso(golden, name):
+    c = C.PISO_CASES[name]
+    W, hd = C.piso_inputs(c)
+    f = dict(int8=R.compute_piso_scales_int8, int4=R.compute_piso_scales_int4,
+             int8_asym=R.compute_piso_scales_int8_asymmetric,
+             int4_asym=R.compute_piso_scales_int4_asymmetric)[c["kind"]]
+    o = f(W, hd)
+    if isinstance(o, tuple):
+        assert np.array_equal(o[0], golden[name + "/scales"])
+        assert np.array_equal(o[1], golden[name + "/zp"])
+    else:
+        assert np.array_equal(o, golden[name + "/scales"])
