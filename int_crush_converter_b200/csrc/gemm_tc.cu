@@ -1,0 +1,390 @@
+// D = beta*C + alpha * A * B^T on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA computes a 128 x BN tile.  Warp roles (256 threads):
+//   warp 0   : TMA producer (one thread) -- K-major fp32 tiles, 128B swizzle
+//   warp 1   : MMA issuer (one thread)   -- tcgen05.mma.kind::tf32, M=128, N=BN, K=8
+//   warp 2   : TMEM allocator
+//   warps 4-7: epilogue -- tcgen05.ld 32x32b, beta*C + alpha*acc, store
+// PASSES = 3 implements 3xTF32: operands arrive as hi/lo pairs (hi exactly
+// TF32) and the accumulator receives hi*hi + hi*lo + lo*hi, giving close to
+// fp32 accuracy (needed by the Hessian inverse and the GPTQ error feedback).
+// Every mbarrier wait is bounded (globaltimer); on timeout the kernel records
+// DEV_TIMEOUT in the device status word and finishes without waiting further.
+// No TMA multicast is used anywhere: every CTA loads its own tiles.
+#include "common.cuh"
+#include "internal.h"
+
+namespace ic {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements per 128-byte swizzle row
+constexpr unsigned long long WAIT_LIMIT_NS = 4000000000ull;  // 4 s
+
+struct GemmArgs {
+  int m, n, k;
+  float alpha, beta;
+  const float* c_hi;
+  const float* c_lo;
+  long long ldc;
+  float* d_hi;
+  float* d_lo;
+  long long ldd;
+  unsigned* flags;
+  int vec;  // C/D rows 16-byte aligned: vectorised epilogue
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and flags a timeout) instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned* flags) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+      atomicOr(flags, DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// UMMA shared-memory descriptor: K-major, 128B swizzle, 8-row core groups
+// 1024 B apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;            // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // SBO
+  d |= (uint64_t)1 << 46;            // version
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+#define IC_TMEM_LD32(taddr, r)                                                                   \
+  asm volatile(                                                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"   \
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"         \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),     \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),  \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),           \
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),           \
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])            \
+      : "r"(taddr))
+
+template <int BN, int PASSES>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (PASSES == 3 ? 2 : 1);
+  static constexpr int STAGES = 196608 / STAGE_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int PASSES>
+__global__ void __launch_bounds__(256, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA_hi,
+                   const __grid_constant__ CUtensorMap tmA_lo,
+                   const __grid_constant__ CUtensorMap tmB_hi,
+                   const __grid_constant__ CUtensorMap tmB_lo, const GemmArgs args) {
+  using C = Cfg<BN, PASSES>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;
+  const int ktiles = (args.k + BK - 1) / BK;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  const uint32_t acc_bar = smem_u32(bars + 2 * STAGES);
+  auto a_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES); };
+  auto b_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES); };
+  auto a_lo = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES); };
+  auto b_lo = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(acc_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int s = kt % STAGES;
+      const uint32_t ph = (kt / STAGES) & 1;
+      if (kt >= STAGES && !mbar_wait(empty_bar(s), ph ^ 1, args.flags)) break;
+      mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
+      tma_load_2d(a_hi(s), &tmA_hi, kt * BK, m0, full_bar(s));
+      tma_load_2d(b_hi(s), &tmB_hi, kt * BK, n0, full_bar(s));
+      if (PASSES == 3) {
+        tma_load_2d(a_lo(s), &tmA_lo, kt * BK, m0, full_bar(s));
+        tma_load_2d(b_lo(s), &tmB_lo, kt * BK, n0, full_bar(s));
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                               ((uint32_t)(BM >> 4) << 24);
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int s = kt % STAGES;
+      const uint32_t ph = (kt / STAGES) & 1;
+      if (!mbar_wait(full_bar(s), ph, args.flags)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+        const uint64_t ah = sdesc(a_hi(s) + off), bh = sdesc(b_hi(s) + off);
+        mma_tf32(tmem, ah, bh, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+        if (PASSES == 3) {
+          const uint64_t al = sdesc(a_lo(s) + off), bl = sdesc(b_lo(s) + off);
+          mma_tf32(tmem, ah, bl, idesc, 1u);
+          mma_tf32(tmem, al, bh, idesc, 1u);
+        }
+      }
+      mma_commit(empty_bar(s));
+    }
+    if (ktiles > 0) mma_commit(acc_bar);
+  } else if (warp >= 4) {
+    // ---------------- epilogue ----------------
+    const int wq = warp - 4;  // TMEM lane quarter this warp may access
+    const int row = m0 + wq * 32 + lane;
+    const bool have_acc = ktiles > 0 && mbar_wait(acc_bar, 0, args.flags);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const bool row_ok = row < args.m;
+#pragma unroll 1
+    for (int cc = 0; cc < BN / 32; ++cc) {
+      uint32_t r[32];
+      if (have_acc) {
+        const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(cc * 32);
+        IC_TMEM_LD32(taddr, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      const int col0 = n0 + cc * 32;
+      if (!row_ok || col0 >= args.n) continue;
+      const float* crow_hi = args.c_hi ? args.c_hi + (long long)row * args.ldc + col0 : nullptr;
+      const float* crow_lo = args.c_lo ? args.c_lo + (long long)row * args.ldc + col0 : nullptr;
+      float* drow_hi = args.d_hi + (long long)row * args.ldd + col0;
+      float* drow_lo = args.d_lo ? args.d_lo + (long long)row * args.ldd + col0 : nullptr;
+      const bool read_c = args.beta != 0.f && crow_hi != nullptr;
+      if (args.vec && col0 + 32 <= args.n) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float v[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = args.alpha * __uint_as_float(r[j4 * 4 + t]);
+          if (read_c) {
+            float4 c = reinterpret_cast<const float4*>(crow_hi)[j4];
+            if (crow_lo) {
+              const float4 cl = reinterpret_cast<const float4*>(crow_lo)[j4];
+              c.x += cl.x; c.y += cl.y; c.z += cl.z; c.w += cl.w;
+            }
+            v[0] = fmaf(args.beta, c.x, v[0]);
+            v[1] = fmaf(args.beta, c.y, v[1]);
+            v[2] = fmaf(args.beta, c.z, v[2]);
+            v[3] = fmaf(args.beta, c.w, v[3]);
+          }
+          if (drow_lo) {
+            float4 h, l;
+            split_tf32(v[0], h.x, l.x);
+            split_tf32(v[1], h.y, l.y);
+            split_tf32(v[2], h.z, l.z);
+            split_tf32(v[3], h.w, l.w);
+            reinterpret_cast<float4*>(drow_hi)[j4] = h;
+            reinterpret_cast<float4*>(drow_lo)[j4] = l;
+          } else {
+            reinterpret_cast<float4*>(drow_hi)[j4] = make_float4(v[0], v[1], v[2], v[3]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (col0 + j >= args.n) continue;
+          float v = args.alpha * __uint_as_float(r[j]);
+          if (read_c) {
+            float c = crow_hi[j];
+            if (crow_lo) c += crow_lo[j];
+            v = fmaf(args.beta, c, v);
+          }
+          if (drow_lo) {
+            float h, l;
+            split_tf32(v, h, l);
+            drow_hi[j] = h;
+            drow_lo[j] = l;
+          } else {
+            drow_hi[j] = v;
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 2) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int make_map(CUtensorMap* tm, const float* base, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(IC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(IC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld k=%lld ld=%lld", (int)r,
+                (long long)rows, (long long)k, (long long)ld);
+  return IC_OK;
+}
+
+template <int BN, int PASSES>
+int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+           const GemmArgs& a, cudaStream_t st) {
+  using C = Cfg<BN, PASSES>;
+  static bool attr = false;
+  if (!attr) {
+    IC_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<BN, PASSES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM));
+    attr = true;
+  }
+  dim3 grid((unsigned)cdiv(a.n, BN), (unsigned)cdiv(a.m, BM));
+  gemm_tn_kernel<BN, PASSES><<<grid, 256, C::SMEM, st>>>(ah, al, bh, bl, a);
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
+            int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
+            const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
+            int64_t ldd, int passes, cudaStream_t st) {
+  if (m <= 0 || n <= 0) return IC_OK;
+  if (passes != 1 && passes != 3) return fail(IC_ERR_INVALID, "gemm: passes must be 1 or 3");
+  if (passes == 3 && (!a_lo || !b_lo)) return fail(IC_ERR_INVALID, "gemm: 3xTF32 needs lo parts");
+  if (!a_hi || !b_hi || !d_hi) return fail(IC_ERR_INVALID, "gemm: null operand");
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "gemm: size");
+  if ((lda | ldb) & 3) return fail(IC_ERR_INVALID, "gemm: A/B leading dimensions must be multiples of 4");
+  if (!aligned16(a_hi) || !aligned16(b_hi) || (passes == 3 && (!aligned16(a_lo) || !aligned16(b_lo))))
+    return fail(IC_ERR_INVALID, "gemm: A/B operands must be 16-byte aligned");
+  const bool vec = !((ldc | ldd) & 3) && aligned16(d_hi) && (!c_hi || aligned16(c_hi)) &&
+                   (!c_lo || aligned16(c_lo)) && (!d_lo || aligned16(d_lo));
+  unsigned* flags = device_flags();
+  if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
+  GemmArgs a{(int)m, (int)n, (int)(k > 0 ? k : 0), alpha, beta, c_hi, c_lo, (long long)ldc,
+             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0};
+  const int64_t kk = k > 0 ? k : 1;
+  CUtensorMap ah, al, bh, bl;
+  if (passes == 3) {
+    IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
+    IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 128));
+    IC_TRY(make_map(&al, a_lo, m, kk, lda, BM));
+    IC_TRY(make_map(&bl, b_lo, n, kk, ldb, 128));
+    return launch<128, 3>(ah, al, bh, bl, a, st);
+  }
+  IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
+  IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 256));
+  return launch<256, 1>(ah, ah, bh, bh, a, st);
+}
+
+}  // namespace ic
+
+extern "C" int ic_gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi,
+                          const float* a_lo, int64_t lda, const float* b_hi, const float* b_lo,
+                          int64_t ldb, float beta, const float* c_hi, const float* c_lo, int64_t ldc,
+                          float* d_hi, float* d_lo, int64_t ldd, int passes, void* stream) {
+  return ic::gemm_tn(m, n, k, alpha, a_hi, a_lo, lda, b_hi, b_lo, ldb, beta, c_hi, c_lo, ldc, d_hi, d_lo,
+                     ldd, passes, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,175 @@
+// Group-wise Hadamard rotation (ConvRot) of weights and Hessians: the row
+// (or a 32-column strip of rot rows) being rotated lives in shared memory,
+// so HBM sees each element once per pass.
+#include <math.h>
+
+#include "common.cuh"
+#include "hadamard.cuh"
+#include "internal.h"
+
+namespace ic {
+namespace {
+
+constexpr int ROT_CHUNK = 8192;  // columns per CTA for the row rotation
+
+template <typename T>
+__global__ void __launch_bounds__(256) rotate_rows_kernel(const T* __restrict__ W, int64_t N, int64_t ldw,
+                                                          int rot, float* __restrict__ out, int64_t ldo,
+                                                          int64_t npad) {
+  __shared__ float s[ROT_CHUNK];
+  const int64_t row = blockIdx.x;
+  const int64_t c0 = (int64_t)blockIdx.y * ROT_CHUNK;
+  const int len = (int)((npad - c0) < ROT_CHUNK ? (npad - c0) : ROT_CHUNK);
+  const T* src = W + row * ldw;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) {
+    const int64_t c = c0 + i;
+    s[i] = c < N ? load_as_f32(src + c) : 0.f;
+  }
+  __syncthreads();
+  hadamard_smem(s, len, rot, 1, 1, 0);
+  float* dst = out + row * ldo + c0;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) dst[i] = s[i];
+}
+
+// Row pass of R^T H R: every row of H gets the group Hadamard along its
+// columns (H R).  Rows >= n and columns >= n are the zero padding.
+__global__ void __launch_bounds__(256) hess_rows_kernel(const float* __restrict__ H, int64_t n, int64_t ldh,
+                                                        int64_t bstride, int rot, float* __restrict__ out,
+                                                        int64_t npad, int64_t ldo, int64_t ostride) {
+  __shared__ float s[ROT_CHUNK];
+  const int64_t row = blockIdx.x;
+  const int64_t b = blockIdx.z;
+  const int64_t c0 = (int64_t)blockIdx.y * ROT_CHUNK;
+  const int len = (int)((npad - c0) < ROT_CHUNK ? (npad - c0) : ROT_CHUNK);
+  const float* src = H + b * bstride + row * ldh;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) {
+    const int64_t c = c0 + i;
+    s[i] = (row < n && c < n) ? src[c] : 0.f;
+  }
+  __syncthreads();
+  hadamard_smem(s, len, rot, 1, 1, 0);
+  float* dst = out + b * ostride + row * ldo + c0;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) dst[i] = s[i];
+}
+
+// Column pass: R^T along the row index within each group of `rot` rows, for a
+// strip of 32 columns; writes a TF32 hi/lo pair when lo != NULL.
+constexpr int COLS = 32;
+__global__ void __launch_bounds__(256) hess_cols_kernel(float* __restrict__ hi, float* __restrict__ lo,
+                                                        int64_t npad, int64_t ldo, int64_t ostride, int rot) {
+  extern __shared__ float tile[];  // [rot][COLS+1]
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * rot;
+  const int64_t c0 = (int64_t)blockIdx.x * COLS;
+  float* base = hi + b * ostride;
+  for (int i = threadIdx.x; i < rot * COLS; i += blockDim.x) {
+    const int r = i / COLS, c = i % COLS;
+    tile[r * (COLS + 1) + c] = (c0 + c < npad) ? base[(r0 + r) * ldo + c0 + c] : 0.f;
+  }
+  __syncthreads();
+  hadamard_smem(tile, rot, rot, COLS + 1, COLS, 1);
+  for (int i = threadIdx.x; i < rot * COLS; i += blockDim.x) {
+    const int r = i / COLS, c = i % COLS;
+    if (c0 + c >= npad) continue;
+    const float v = tile[r * (COLS + 1) + c];
+    const int64_t idx = b * ostride + (r0 + r) * ldo + c0 + c;
+    if (lo) {
+      const float h = to_tf32(v);
+      hi[idx] = h;
+      lo[idx] = __fsub_rn(v, h);
+    } else {
+      hi[idx] = v;
+    }
+  }
+}
+
+__global__ void split_kernel(const float* __restrict__ in, int64_t rows, int64_t cols, int64_t ldi,
+                             float* __restrict__ hi, float* __restrict__ lo, int64_t ldo) {
+  const int64_t total = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    const float v = in[r * ldi + c];
+    const float h = to_tf32(v);
+    hi[r * ldo + c] = h;
+    if (lo) lo[r * ldo + c] = __fsub_rn(v, h);
+  }
+}
+
+bool rot_ok(int rot) { return rot == 0 || (rot >= 2 && rot <= 1024 && (rot & (rot - 1)) == 0); }
+
+}  // namespace
+
+int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot, float* out,
+                   int64_t ldo, cudaStream_t st) {
+  if (!rot_ok(rot)) return fail(IC_ERR_INVALID, "rot_size must be a power of 2, got %d", rot);
+  if (M < 0 || N < 0 || ldw < N) return fail(IC_ERR_INVALID, "rotate_weights: bad shape");
+  const int r = rot ? rot : 1;
+  const int64_t npad = cdiv(N, r) * r;
+  if (ldo < npad) return fail(IC_ERR_INVALID, "rotate_weights: ldo < padded width");
+  if (M == 0 || npad == 0) return IC_OK;
+  if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_weights: too many rows");
+  dim3 grid((unsigned)M, (unsigned)cdiv(npad, ROT_CHUNK));
+  switch (dtype) {
+    case IC_F32: rotate_rows_kernel<float><<<grid, 256, 0, st>>>((const float*)W, N, ldw, r, out, ldo, npad); break;
+    case IC_F16: rotate_rows_kernel<__half><<<grid, 256, 0, st>>>((const __half*)W, N, ldw, r, out, ldo, npad); break;
+    case IC_BF16:
+      rotate_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)W, N, ldw, r, out, ldo, npad);
+      break;
+    default: return fail(IC_ERR_INVALID, "rotate_weights: unknown dtype %d", dtype);
+  }
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
+
+int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int rot, float* out_hi,
+                   float* out_lo, int64_t npad, int64_t ldo, cudaStream_t st) {
+  if (!rot_ok(rot)) return fail(IC_ERR_INVALID, "rot_size must be a power of 2, got %d", rot);
+  const int r = rot ? rot : 1;
+  if (nbatch < 1 || n <= 0 || ldh < n) return fail(IC_ERR_INVALID, "rotate_hessian: bad shape");
+  if (npad != cdiv(n, r) * r) return fail(IC_ERR_INVALID, "rotate_hessian: npad mismatch");
+  if (ldo < npad) return fail(IC_ERR_INVALID, "rotate_hessian: ldo < npad");
+  if (nbatch > 1 && n % r)
+    return fail(IC_ERR_INVALID, "Block size %lld is not divisible by rot_size %d", (long long)n, rot);
+  if (npad > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_hessian: too large");
+  const int64_t ostride = npad * ldo;
+  dim3 g1((unsigned)npad, (unsigned)cdiv(npad, ROT_CHUNK), (unsigned)nbatch);
+  hess_rows_kernel<<<g1, 256, 0, st>>>(H, n, ldh, n * ldh, r, out_hi, npad, ldo, ostride);
+  IC_CHECK_LAUNCH();
+  if (r > 1) {
+    const size_t sm = (size_t)r * (COLS + 1) * 4;
+    if (sm > 48 * 1024)
+      IC_CUDA(cudaFuncSetAttribute(hess_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    dim3 g2((unsigned)cdiv(npad, COLS), (unsigned)(npad / r), (unsigned)nbatch);
+    hess_cols_kernel<<<g2, 256, sm, st>>>(out_hi, out_lo, npad, ldo, ostride, r);
+    IC_CHECK_LAUNCH();
+  } else if (out_lo) {
+    IC_TRY(split_tf32(out_hi, nbatch * npad, npad, ldo, out_hi, out_lo, ldo, st));
+  }
+  return IC_OK;
+}
+
+int split_tf32(const float* in, int64_t rows, int64_t cols, int64_t ldi, float* hi, float* lo, int64_t ldo,
+               cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return IC_OK;
+  const int64_t total = rows * cols;
+  const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 148 * 16);
+  split_kernel<<<blocks, 256, 0, st>>>(in, rows, cols, ldi, hi, lo, ldo);
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
+
+}  // namespace ic
+
+extern "C" int ic_rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot,
+                                 float* out, int64_t ldo, void* stream) {
+  return ic::rotate_weights(W, dtype, M, N, ldw, rot, out, ldo, (cudaStream_t)stream);
+}
+extern "C" int ic_rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int rot,
+                                 float* out_hi, float* out_lo, int64_t npad, void* stream) {
+  return ic::rotate_hessian(H, nbatch, n, ldh, rot, out_hi, out_lo, npad, npad, (cudaStream_t)stream);
+}
+extern "C" int ic_split_tf32(const float* in, int64_t rows, int64_t cols, int64_t ldi, float* out_hi,
+                             float* out_lo, int64_t ldo, void* stream) {
+  return ic::split_tf32(in, rows, cols, ldi, out_hi, out_lo, ldo, (cudaStream_t)stream);
+}

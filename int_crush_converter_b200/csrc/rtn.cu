@@ -1,0 +1,350 @@
+// Round-to-nearest quantization: per-group scale search, codes, INT4 packing
+// and the pipeline's verify statistics, one CTA per weight row with the
+// (optionally rotated) row resident in shared memory, so HBM sees each weight
+// once: read fp16/bf16/fp32, write codes + scales.
+//
+// Arithmetic follows converter/scales.py operation by operation (fp32 IEEE,
+// no contraction): scale = clamp(stat * ratio / divisor), fp16 storage,
+// candidate MSE with round-half-even (Tensor.round), final codes with
+// round-half-away-from-zero, strict-< ratio selection (first ratio wins ties).
+#include "common.cuh"
+#include "hadamard.cuh"
+#include "internal.h"
+
+namespace ic {
+namespace {
+
+constexpr int NT = 256;
+constexpr int MAX_RATIOS = 32;
+constexpr int64_t MAX_ROW = 49152;  // fp32 elements of one row in shared memory
+
+struct RtnArgs {
+  const void* W;
+  int dtype;
+  int64_t N, ldw, npad, gs;
+  int rot, bits, asym, G, nratios, given, zero_group_zp0;
+  float ratios[MAX_RATIOS];
+  const uint16_t* in_scales;
+  const int8_t* in_zp;
+  uint16_t* scales;
+  int8_t* zp;
+  int8_t* codes;
+  int64_t ldc;
+  uint8_t* packed;
+  int64_t ldp;
+  double* row_sqerr;
+  float* row_maxerr;
+};
+
+// Reduction over a "team": the whole CTA (CTA=true) or one warp.
+template <bool CTA>
+struct Team {
+  float* red;  // >= 32 floats of shared scratch (CTA teams only)
+  __device__ int rank() const { return CTA ? (int)threadIdx.x : (int)(threadIdx.x & 31); }
+  __device__ int size() const { return CTA ? (int)blockDim.x : 32; }
+  template <typename Op>
+  __device__ float reduce(float v, Op op) const {
+    for (int o = 16; o; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (!CTA) return v;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = op(r, red[w]);
+    return r;
+  }
+};
+
+struct OpMax { __device__ float operator()(float a, float b) const { return nmax(a, b); } };
+struct OpMin { __device__ float operator()(float a, float b) const { return nmin(a, b); } };
+struct OpSum { __device__ float operator()(float a, float b) const { return __fadd_rn(a, b); } };
+
+__device__ __forceinline__ float clamp_scale(float s) { return clampf(s, 1e-5f, 65500.f); }
+
+// converter/scales.py:184-229
+__device__ __forceinline__ float fix_asym(float s, float wmin, float wmax, float qmin, float qmax) {
+  const float spread = qmax - qmin;
+  const float zr = __fsub_rn(qmin, rhaz(__fdiv_rn(wmin, s)));
+  if (zr < qmin) s = fmaxf(s, clamp_scale(__fdiv_rn(wmax, spread)));
+  if (zr > qmax) s = fmaxf(s, clamp_scale(__fdiv_rn(-wmin, spread)));
+  return s;
+}
+
+template <bool CTA>
+__device__ void process_group(const float* x, int len, const RtnArgs& a, int64_t row, int g, Team<CTA> team,
+                              double& sq_acc, float& max_acc) {
+  const float qmin = a.bits == 4 ? -8.f : -128.f;
+  const float qmax = a.bits == 4 ? 7.f : 127.f;
+  const int t = team.rank(), T = team.size();
+  float s = 0.f, zp = 0.f;
+  uint16_t s16;
+  if (a.given) {
+    s16 = a.in_scales[row * a.G + g];
+    zp = a.asym ? (float)a.in_zp[row * a.G + g] : 0.f;
+  } else {
+    float amax = 0.f, wmin = __int_as_float(0x7f800000), wmax = __int_as_float(0xff800000);
+    for (int i = t; i < len; i += T) {
+      const float v = x[i];
+      amax = nmax(amax, fabsf(v));
+      wmin = nmin(wmin, v);
+      wmax = nmax(wmax, v);
+    }
+    if (a.asym) {
+      wmin = team.reduce(wmin, OpMin());
+      wmax = team.reduce(wmax, OpMax());
+    } else {
+      amax = team.reduce(amax, OpMax());
+    }
+    const float div = a.asym ? (qmax - qmin) : (a.bits == 4 ? 7.f : 127.f);
+    if (a.nratios == 0) {
+      if (a.asym) {
+        s = clamp_scale(__fdiv_rn(__fsub_rn(wmax, wmin), div));
+        s = fix_asym(s, wmin, wmax, qmin, qmax);
+        zp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, s))), qmin, qmax);
+        if (a.zero_group_zp0 && wmin == 0.f && wmax == 0.f) zp = 0.f;
+      } else {
+        s = clamp_scale(__fdiv_rn(amax, div));
+      }
+    } else {
+      float best_mse = 0.f;
+      for (int r = 0; r < a.nratios; ++r) {
+        const float ratio = a.ratios[r];
+        float cs, czp = 0.f;
+        if (a.asym) {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(__fsub_rn(wmax, wmin), ratio), div));
+          cs = fix_asym(cs, wmin, wmax, qmin, qmax);
+          czp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, cs))), qmin, qmax);
+        } else {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(amax, ratio), div));
+        }
+        float part = 0.f;
+        for (int i = t; i < len; i += T) {
+          const float v = x[i];
+          float y = __fdiv_rn(v, cs);
+          if (a.asym) y = __fadd_rn(y, czp);
+          const float q = clampf(rintf(y), qmin, qmax);
+          const float deq = a.asym ? __fmul_rn(__fsub_rn(q, czp), cs) : __fmul_rn(q, cs);
+          const float e = __fsub_rn(v, deq);
+          part = __fadd_rn(part, __fmul_rn(e, e));
+        }
+        const float mse = __fdiv_rn(team.reduce(part, OpSum()), (float)len);
+        if (r == 0 || mse < best_mse) {
+          best_mse = mse;
+          s = cs;
+          zp = czp;
+        }
+      }
+    }
+    s16 = __half_as_ushort(__float2half_rn(s));
+    if (t == 0) {
+      if (a.scales) a.scales[row * a.G + g] = s16;
+      if (a.zp && a.asym) a.zp[row * a.G + g] = (int8_t)zp;
+    }
+  }
+  if (!(a.codes || a.packed || a.row_sqerr || a.row_maxerr)) return;
+  const float sf = __half2float(__ushort_as_half(s16));
+  const int64_t col0 = (int64_t)g * a.gs;
+  // two adjacent columns per step so a thread owns whole packed bytes
+  for (int i = 2 * t; i < len; i += 2 * T) {
+    float qv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (i + u >= len) {
+        qv[u] = 0.f;
+        continue;
+      }
+      const float v = x[i + u];
+      float y = __fdiv_rn(v, sf);
+      if (a.asym) y = __fadd_rn(y, zp);
+      const float q = clampf(rhaz(y), qmin, qmax);
+      qv[u] = q;
+      if (a.codes) a.codes[row * a.ldc + col0 + i + u] = (int8_t)q;
+      // verify statistics over the rotated, padded W_work (pipeline.py:919-931)
+      const float deq = a.asym ? __fmul_rn(__fsub_rn(q, zp), sf) : __fmul_rn(q, sf);
+      const float d = __fsub_rn(v, deq);
+      sq_acc += (double)d * (double)d;
+      max_acc = nmax(max_acc, fabsf(d));
+    }
+    if (a.packed) {
+      const int lo = (int)qv[0] & 15, hi = (int)qv[1] & 15;
+      a.packed[row * a.ldp + (col0 + i) / 2] = (uint8_t)(lo | (hi << 4));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NT) rtn_row_kernel(const RtnArgs a) {
+  extern __shared__ float row_s[];
+  __shared__ float red[32];
+  __shared__ double red_d[32];
+  const int64_t row = blockIdx.x;
+  for (int64_t i = threadIdx.x; i < a.npad; i += NT) {
+    float v = 0.f;
+    if (i < a.N) {
+      if (a.dtype == IC_F16) v = __half2float(reinterpret_cast<const __half*>(a.W)[row * a.ldw + i]);
+      else if (a.dtype == IC_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.W)[row * a.ldw + i]);
+      else v = reinterpret_cast<const float*>(a.W)[row * a.ldw + i];
+    }
+    row_s[i] = v;
+  }
+  __syncthreads();
+  if (a.rot > 1) hadamard_smem(row_s, (int)a.npad, a.rot, 1, 1, 0);
+  double sq = 0.0;
+  float mx = 0.f;
+  if (a.G == 1) {
+    Team<true> team{red};
+    process_group<true>(row_s, (int)a.npad, a, row, 0, team, sq, mx);
+  } else {
+    Team<false> team{nullptr};
+    for (int g = threadIdx.x >> 5; g < a.G; g += NT / 32)
+      process_group<false>(row_s + (int64_t)g * a.gs, (int)a.gs, a, row, g, team, sq, mx);
+  }
+  if (a.row_sqerr || a.row_maxerr) {
+    sq = warp_sum_d(sq);
+    for (int o = 16; o; o >>= 1) mx = nmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+      red_d[threadIdx.x >> 5] = sq;
+      red[threadIdx.x >> 5] = mx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double s = 0.0;
+      float m = 0.f;
+      for (int w = 0; w < NT / 32; ++w) {
+        s += red_d[w];
+        m = nmax(m, red[w]);
+      }
+      if (a.row_sqerr) a.row_sqerr[row] = s;
+      if (a.row_maxerr) a.row_maxerr[row] = m;
+    }
+  }
+}
+
+__global__ void pack_kernel(const int8_t* __restrict__ codes, int64_t M, int64_t K, int64_t ldc,
+                            uint8_t* __restrict__ packed, int64_t ldp, unsigned* flags) {
+  const int64_t kp = (K + 1) / 2;
+  const int64_t total = M * kp;
+  bool bad = false;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / kp, b = i % kp;
+    const int c0 = codes[r * ldc + 2 * b];
+    const int c1 = (2 * b + 1 < K) ? codes[r * ldc + 2 * b + 1] : 0;
+    bad |= (c0 < -8 || c0 > 7 || c1 < -8 || c1 > 7);
+    packed[r * ldp + b] = (uint8_t)((c0 & 15) | ((c1 & 15) << 4));
+  }
+  if (bad) atomicOr(flags, DEV_RANGE);
+}
+
+__global__ void unpack_kernel(const uint8_t* __restrict__ packed, int64_t M, int64_t K, int64_t ldp,
+                              int8_t* __restrict__ codes, int64_t ldc) {
+  const int64_t total = M * K;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K, c = i % K;
+    const int b = packed[r * ldp + c / 2];
+    const int v = (c & 1) ? (b >> 4) & 15 : b & 15;
+    codes[r * ldc + c] = (int8_t)(v >= 8 ? v - 16 : v);
+  }
+}
+
+int launch_rtn(RtnArgs& a, int64_t M, cudaStream_t st) {
+  if (M == 0 || a.npad == 0) return IC_OK;
+  if (a.npad > MAX_ROW)
+    return fail(IC_ERR_UNSUPPORTED, "rtn: row of %lld elements exceeds %lld", (long long)a.npad, (long long)MAX_ROW);
+  if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rtn: too many rows");
+  static bool attr = false;
+  if (!attr) {
+    IC_CUDA(cudaFuncSetAttribute(rtn_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(MAX_ROW * 4)));
+    attr = true;
+  }
+  rtn_row_kernel<<<(unsigned)M, NT, (size_t)a.npad * 4, st>>>(a);
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
+
+int fill_ratios(RtnArgs& a, const float* ratios, int nratios) {
+  if (nratios < 0 || nratios > MAX_RATIOS)
+    return fail(IC_ERR_UNSUPPORTED, "rtn: at most %d clipping ratios", MAX_RATIOS);
+  a.nratios = ratios ? nratios : 0;
+  for (int i = 0; i < a.nratios; ++i) a.ratios[i] = ratios[i];
+  return IC_OK;
+}
+
+int64_t grid_elems(int64_t n) { return std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), 148 * 32)); }
+
+}  // namespace
+}  // namespace ic
+
+using namespace ic;
+
+extern "C" int ic_rtn_scales(const float* W, int64_t M, int64_t N, int64_t ldw, int bits, int asym,
+                             int64_t group_size, const float* ratios, int nratios, uint16_t* scales_f16,
+                             int8_t* zp, void* stream) {
+  if (bits != 4 && bits != 8) return fail(IC_ERR_INVALID, "int_bits must be 4 or 8, got %d", bits);
+  if (group_size <= 0 || N % group_size) return fail(IC_ERR_INVALID, "rtn_scales: N must be a multiple of group_size");
+  if (bits == 8 && group_size != N) return fail(IC_ERR_INVALID, "rtn_scales: INT8 scales are per row");
+  if (asym && !zp) return fail(IC_ERR_INVALID, "rtn_scales: asymmetric needs a zero-point output");
+  RtnArgs a{};
+  a.W = W; a.dtype = IC_F32; a.N = N; a.ldw = ldw; a.npad = N; a.gs = group_size;
+  a.rot = 0; a.bits = bits; a.asym = asym; a.G = (int)(N / group_size); a.given = 0;
+  a.zero_group_zp0 = (bits == 4);
+  a.scales = scales_f16; a.zp = zp;
+  IC_TRY(fill_ratios(a, ratios, nratios));
+  return launch_rtn(a, M, (cudaStream_t)stream);
+}
+
+extern "C" int ic_rtn_codes(const float* W, int64_t M, int64_t N, int64_t ldw, int bits, int asym,
+                            int64_t group_size, const uint16_t* scales_f16, const int8_t* zp, int8_t* codes,
+                            int64_t ldc, void* stream) {
+  if (bits != 4 && bits != 8) return fail(IC_ERR_INVALID, "int_bits must be 4 or 8, got %d", bits);
+  if (group_size <= 0 || N % group_size) return fail(IC_ERR_INVALID, "rtn_codes: N must be a multiple of group_size");
+  if (asym && !zp) return fail(IC_ERR_INVALID, "rtn_codes: asymmetric needs zero-points");
+  RtnArgs a{};
+  a.W = W; a.dtype = IC_F32; a.N = N; a.ldw = ldw; a.npad = N; a.gs = group_size;
+  a.rot = 0; a.bits = bits; a.asym = asym; a.G = (int)(N / group_size); a.given = 1;
+  a.in_scales = scales_f16; a.in_zp = zp; a.codes = codes; a.ldc = ldc;
+  return launch_rtn(a, M, (cudaStream_t)stream);
+}
+
+extern "C" int ic_rtn_fused(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot, int bits,
+                            int asym, const float* ratios, int nratios, int8_t* codes, uint8_t* packed,
+                            uint16_t* scales_f16, int8_t* zp, double* row_sqerr, float* row_maxerr,
+                            void* stream) {
+  if (bits != 4 && bits != 8) return fail(IC_ERR_INVALID, "int_bits must be 4 or 8, got %d", bits);
+  if (rot != 0 && (rot < 2 || rot > 1024 || (rot & (rot - 1))))
+    return fail(IC_ERR_INVALID, "rot_size must be a power of 2, got %d", rot);
+  if (packed && bits != 4) return fail(IC_ERR_INVALID, "rtn_fused: packing is INT4 only");
+  if (dtype != IC_F32 && dtype != IC_F16 && dtype != IC_BF16) return fail(IC_ERR_INVALID, "rtn_fused: dtype");
+  const int r = rot ? rot : 1;
+  RtnArgs a{};
+  a.W = W; a.dtype = dtype; a.N = N; a.ldw = ldw; a.npad = cdiv(N, r) * r; a.gs = a.npad;
+  a.rot = rot; a.bits = bits; a.asym = asym; a.G = 1; a.given = 0;
+  a.zero_group_zp0 = (bits == 4);
+  a.scales = scales_f16; a.zp = zp; a.codes = codes; a.ldc = a.npad; a.packed = packed;
+  a.ldp = (a.npad + 1) / 2; a.row_sqerr = row_sqerr; a.row_maxerr = row_maxerr;
+  IC_TRY(fill_ratios(a, ratios, nratios));
+  return launch_rtn(a, M, (cudaStream_t)stream);
+}
+
+extern "C" int ic_pack_int4(const int8_t* codes, int64_t M, int64_t K, int64_t ldc, uint8_t* packed, int64_t ldp,
+                            void* stream) {
+  if (M == 0 || K == 0) return IC_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned* flags = device_flags();
+  if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
+  unsigned before = 0;
+  IC_TRY(read_and_clear_flags(&before, st));
+  pack_kernel<<<(int)grid_elems(M * ((K + 1) / 2)), 256, 0, st>>>(codes, M, K, ldc, packed, ldp, flags);
+  IC_CHECK_LAUNCH();
+  unsigned after = 0;
+  IC_TRY(read_and_clear_flags(&after, st));
+  if (after & DEV_RANGE) return fail(IC_ERR_RANGE, "Values must be in [-8, 7]");
+  return IC_OK;
+}
+
+extern "C" int ic_unpack_int4(const uint8_t* packed, int64_t M, int64_t K, int64_t ldp, int8_t* codes, int64_t ldc,
+                              void* stream) {
+  if (M == 0 || K == 0) return IC_OK;
+  unpack_kernel<<<(int)grid_elems(M * K), 256, 0, (cudaStream_t)stream>>>(packed, M, K, ldp, codes, ldc);
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
