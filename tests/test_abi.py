@@ -1,0 +1,32 @@
+"""The C-ABI library loads and exports every symbol include/intcrush_b200.h declares (no GPU needed)."""
+
+import ctypes
+import os
+import re
+
+from int_crush_converter_b200 import _native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    src = open(os.path.join(ROOT, "include", "intcrush_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ic_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_symbols_exported():
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    names = declared()
+    assert len(names) >= 25
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_binding_covers_header():
+    assert set(declared()) == set(_native.SIGNATURES)
+
+
+def test_version_and_no_device():
+    lib = _native.load()
+    assert b"sm_100a" in lib.ic_version()
