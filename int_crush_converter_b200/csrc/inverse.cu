@@ -1,17 +1,17 @@
 // Damped inverse of an SPD Hessian on the GPU, replacing gptq._prepare_hinv
 // (converter/gptq.py:113-121) + the Cholesky branch of rounding._invert_hessian
-// (rounding.py:19-34).
+// (rounding.py:19-34: torch.linalg.cholesky + torch.cholesky_inverse).
 //
-// H = [A B; B^T D] is inverted by the block Schur-complement recursion
-//   Ai = A^-1, Ct = B^T Ai, S = D - B^T Ai B, Si = S^-1,
-//   H^-1 = [Ai + C Si C^T, -C Si; -Si C^T, Si]   (C = Ct^T)
-// which is block LDL^T elimination without pivoting (stable for SPD).  All
-// O(n^3) work is D = beta*C + alpha*A*B^T products on the tcgen05 tensor
-// cores in 3xTF32; matrices are held as TF32 hi/lo pairs whose sum is the
-// exact fp32 value.  Only the lower triangle of the input is ever read (as
-// LAPACK's lower Cholesky does).  Diagonal blocks of <= 128 are inverted in
-// shared memory by Gauss-Jordan elimination; a non-positive pivot sets
-// DEV_NOT_PD.
+// Same algorithm family as LAPACK potrf + potri, recursive and GEMM-rich:
+//   1. L = chol(H), recursive:      L11 = chol(A11); L21 = A21 L11^-T (recursive
+//      triangular solve); A22 -= L21 L21^T; L22 = chol(A22)
+//   2. U = L^-T (upper), recursive: U12 = (-U11 L21^T) L22^-T
+//   3. H^-1 = U U^T
+// Every O(n^3) step is D = beta*C + alpha*A*B^T on the tcgen05 tensor cores in
+// 3xTF32 (matrices held as TF32 hi/lo pairs whose sum is the exact fp32
+// value).  Only the 128 x 128 diagonal blocks are factored in shared memory;
+// their explicit inverses serve the leaves of the triangular solves.  Only
+// the lower triangle of H is read.  A non-positive pivot sets DEV_NOT_PD.
 #include "common.cuh"
 #include "internal.h"
 
@@ -19,7 +19,8 @@ namespace ic {
 namespace {
 
 constexpr int BASE = 128;
-constexpr size_t GJ_SMEM = (size_t)(BASE * (BASE + 1) + 2 * BASE) * 4;
+constexpr int LDS = BASE + 1;
+constexpr size_t BASE_SMEM = (size_t)2 * BASE * LDS * 4;
 
 // H += lambda*I, lambda = damping * max(mean(diag H), 1e-6)  (gptq.py:118-119)
 __global__ void __launch_bounds__(1024) damp_kernel(float* hi, float* lo, int64_t n, int64_t ld, float damping) {
@@ -45,49 +46,76 @@ __global__ void __launch_bounds__(1024) damp_kernel(float* hi, float* lo, int64_
   }
 }
 
-// In-place Gauss-Jordan inverse of one n x n (n <= 128) SPD block, read from
-// the lower triangle, written back full and symmetric.
-__global__ void __launch_bounds__(512) gj_inverse_kernel(float* hi, float* lo, int n, int64_t ld, unsigned* flags) {
-  extern __shared__ float gj_smem[];
-  float(*a)[BASE + 1] = reinterpret_cast<float(*)[BASE + 1]>(gj_smem);
-  float* colk = gj_smem + BASE * (BASE + 1);
-  float* rowk = colk + BASE;
+__device__ __forceinline__ void put_pair(float* hi, float* lo, int64_t idx, float v) {
+  const float h = to_tf32(v);
+  hi[idx] = h;
+  lo[idx] = __fsub_rn(v, h);
+}
+
+// Cholesky of one n x n (n <= 128) diagonal block (lower triangle read), in
+// place (lower L, upper zeroed), plus its explicit inverse Linv (lower) written
+// to the slot [128 x 128].  Inner products accumulate in fp64.
+__global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, int n, int64_t ld, float* ihi,
+                                                        float* ilo, unsigned* flags) {
+  extern __shared__ float sm[];
+  float* a = sm;             // [BASE][LDS]  L
+  float* x = sm + BASE * LDS;  // [BASE][LDS]  Linv
   __shared__ int bad;
   if (threadIdx.x == 0) bad = 0;
   for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
     const int i = idx / n, j = idx % n;
-    const int r = i >= j ? i : j, c = i >= j ? j : i;
-    a[i][j] = __fadd_rn(hi[r * ld + c], lo[r * ld + c]);
+    a[i * LDS + j] = i >= j ? __fadd_rn(hi[i * ld + j], lo[i * ld + j]) : 0.f;
   }
   __syncthreads();
+  // left-looking column Cholesky: column k computed after columns < k
   for (int k = 0; k < n; ++k) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      colk[i] = a[i][k];
-      rowk[i] = a[k][i];
+    // diagonal
+    if (threadIdx.x < 32) {
+      double s = 0.0;
+      for (int t = threadIdx.x; t < k; t += 32) s += (double)a[k * LDS + t] * a[k * LDS + t];
+      s = warp_sum_d(s);
+      if (threadIdx.x == 0) {
+        const double d = (double)a[k * LDS + k] - s;
+        if (!(d > 0.0) || !isfinite(d)) {
+          bad = 1;
+          a[k * LDS + k] = 1.f;
+        } else {
+          a[k * LDS + k] = (float)sqrt(d);
+        }
+      }
     }
     __syncthreads();
-    const float piv = colk[k];
-    if (!(piv > 0.f) || !isfinite(piv)) {
-      if (threadIdx.x == 0) bad = 1;
-    }
-    const float inv = 1.0f / piv;
-    for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
-      const int i = idx / n, j = idx % n;
-      float v;
-      if (i == k && j == k) v = inv;
-      else if (i == k) v = rowk[j] * inv;
-      else if (j == k) v = -colk[i] * inv;
-      else v = a[i][j] - colk[i] * (rowk[j] * inv);
-      a[i][j] = v;
+    const float dkk = a[k * LDS + k];
+    // column below the diagonal: one warp per row
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int i = k + 1 + warp; i < n; i += nw) {
+      double s = 0.0;
+      for (int t = lane; t < k; t += 32) s += (double)a[i * LDS + t] * a[k * LDS + t];
+      s = warp_sum_d(s);
+      if (lane == 0) a[i * LDS + k] = (float)(((double)a[i * LDS + k] - s) / (double)dkk);
     }
     __syncthreads();
   }
+  // Linv: forward substitution, one thread per column c of the identity
+  for (int c = threadIdx.x; c < n; c += blockDim.x) {
+    for (int i = 0; i < n; ++i) {
+      if (i < c) {
+        x[i * LDS + c] = 0.f;
+        continue;
+      }
+      double s = (i == c) ? 1.0 : 0.0;
+      for (int t = c; t < i; ++t) s -= (double)a[i * LDS + t] * x[t * LDS + c];
+      x[i * LDS + c] = (float)(s / (double)a[i * LDS + i]);
+    }
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
     const int i = idx / n, j = idx % n;
-    const float v = 0.5f * (a[i][j] + a[j][i]);
-    const float h = to_tf32(v);
-    hi[i * ld + j] = h;
-    lo[i * ld + j] = __fsub_rn(v, h);
+    put_pair(hi, lo, (int64_t)i * ld + j, i >= j ? a[i * LDS + j] : 0.f);
+  }
+  for (int idx = threadIdx.x; idx < BASE * BASE; idx += blockDim.x) {
+    const int i = idx / BASE, j = idx % BASE;
+    put_pair(ihi, ilo, idx, (i < n && j < n) ? x[i * LDS + j] : 0.f);
   }
   if (threadIdx.x == 0 && bad) atomicOr(flags, DEV_NOT_PD);
 }
@@ -112,28 +140,21 @@ __global__ void transpose_kernel(const float* __restrict__ ih, const float* __re
     const int64_t orow = c0 + dy, ocol = r0 + threadIdx.x;  // out is [cols x rows]
     if (orow < cols && ocol < rows) {
       const float v = __fmul_rn(alpha, t[threadIdx.x][dy]);
-      if (ol) {
-        const float h = to_tf32(v);
-        oh[orow * ldo + ocol] = h;
-        ol[orow * ldo + ocol] = __fsub_rn(v, h);
-      } else {
-        oh[orow * ldo + ocol] = v;
-      }
+      if (ol) put_pair(oh, ol, orow * ldo + ocol, v);
+      else oh[orow * ldo + ocol] = v;
     }
   }
 }
 
-// out = alpha * in on hi/lo pairs
-__global__ void scale_copy_kernel(const float* __restrict__ ih, const float* __restrict__ il, int64_t rows,
-                                  int64_t cols, int64_t ldi, float alpha, float* __restrict__ oh,
-                                  float* __restrict__ ol, int64_t ldo) {
+// copy a [rows x cols] hi/lo block (ldi -> ldo)
+__global__ void copy_pair_kernel(const float* __restrict__ ih, const float* __restrict__ il, int64_t rows,
+                                 int64_t cols, int64_t ldi, float* __restrict__ oh, float* __restrict__ ol,
+                                 int64_t ldo) {
   const int64_t total = rows * cols;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
-    const float v = __fmul_rn(alpha, __fadd_rn(ih[r * ldi + c], il[r * ldi + c]));
-    const float h = to_tf32(v);
-    oh[r * ldo + c] = h;
-    ol[r * ldo + c] = __fsub_rn(v, h);
+    oh[r * ldo + c] = ih[r * ldi + c];
+    ol[r * ldo + c] = il[r * ldi + c];
   }
 }
 
@@ -143,63 +164,95 @@ struct Pair {
   Pair at(int64_t r, int64_t c, int64_t ld) const { return {hi + r * ld + c, lo + r * ld + c}; }
 };
 
-int scale_copy(Pair in, int64_t rows, int64_t cols, int64_t ldi, float alpha, Pair out, int64_t ldo,
-               cudaStream_t st) {
-  const int blocks = (int)std::min<int64_t>(cdiv(rows * cols, 256), 148 * 16);
-  scale_copy_kernel<<<blocks, 256, 0, st>>>(in.hi, in.lo, rows, cols, ldi, alpha, out.hi, out.lo, ldo);
-  IC_CHECK_LAUNCH();
-  return IC_OK;
-}
+struct Ctx {
+  Pair H;        // factor / result, leading dimension ld
+  int64_t ld;
+  Pair U;        // L^-T, leading dimension ld
+  Pair Linv;     // ceil(n/128) slots of [128 x 128]
+  Pair T;        // trsm leaf scratch [n x 128]
+  unsigned* flags;
+  cudaStream_t st;
+  Pair slot(int64_t off) const { return Linv.at((off / BASE) * BASE, 0, BASE); }
+};
 
 int64_t split_point(int64_t n) { return std::max<int64_t>((n / 2 / BASE) * BASE, BASE); }
-int64_t round4(int64_t x) { return (x + 3) & ~int64_t(3); }
 
-// Recursive in-place inverse of the n x n SPD block at A (leading dimension ld).
-int inv_rec(Pair A, int64_t n, int64_t ld, Pair T1, Pair T2, unsigned* flags, cudaStream_t st) {
+int gemm3(const Ctx& c, int64_t m, int64_t n, int64_t k, float alpha, Pair A, int64_t lda, Pair B, int64_t ldb,
+          float beta, Pair D, int64_t ldd, bool c_is_d) {
+  return gemm_tn(m, n, k, alpha, A.hi, A.lo, lda, B.hi, B.lo, ldb, beta, c_is_d ? D.hi : nullptr,
+                 c_is_d ? D.lo : nullptr, ldd, D.hi, D.lo, ldd, 3, c.st);
+}
+
+// X [m x n] (leading dimension ldx) <- X * L^-T, L = the factor's diagonal block at off (size n)
+int trsm_rec(const Ctx& c, Pair X, int64_t m, int64_t ldx, int64_t off, int64_t n) {
+  if (m <= 0 || n <= 0) return IC_OK;
   if (n <= BASE) {
-    static bool attr = false;
-    if (!attr) {
-      IC_CUDA(cudaFuncSetAttribute(gj_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GJ_SMEM));
-      attr = true;
-    }
-    gj_inverse_kernel<<<1, 512, GJ_SMEM, st>>>(A.hi, A.lo, (int)n, ld, flags);
+    IC_TRY(gemm3(c, m, n, n, 1.f, X, ldx, c.slot(off), BASE, 0.f, c.T, BASE, false));
+    const int blocks = (int)std::min<int64_t>(cdiv(m * n, 256), 148 * 16);
+    copy_pair_kernel<<<blocks, 256, 0, c.st>>>(c.T.hi, c.T.lo, m, n, BASE, X.hi, X.lo, ldx);
     IC_CHECK_LAUNCH();
     return IC_OK;
   }
-  const int64_t n1 = split_point(n);
-  const int64_t n2 = n - n1;
-  const int64_t ld2 = round4(n2);  // TMA needs 16-byte row strides
-  Pair H11 = A, H12 = A.at(0, n1, ld), H21 = A.at(n1, 0, ld), H22 = A.at(n1, n1, ld);
-  IC_TRY(inv_rec(H11, n1, ld, T1, T2, flags, st));  // H11 <- Ai
-  // T1 [n2 x n1] = H21 * Ai^T   (Ct = B^T Ai)
-  IC_TRY(gemm_tn(n2, n1, n1, 1.f, H21.hi, H21.lo, ld, H11.hi, H11.lo, ld, 0.f, nullptr, nullptr, n1, T1.hi,
-                 T1.lo, n1, 3, st));
-  // H22 <- S = H22 - H21 * T1^T
-  IC_TRY(gemm_tn(n2, n2, n1, -1.f, H21.hi, H21.lo, ld, T1.hi, T1.lo, n1, 1.f, H22.hi, H22.lo, ld, H22.hi,
-                 H22.lo, ld, 3, st));
-  // H12 <- C = T1^T  [n1 x n2]
-  IC_TRY(transpose(T1.hi, T1.lo, n2, n1, n1, 1.f, H12.hi, H12.lo, ld, st));
-  IC_TRY(inv_rec(H22, n2, ld, T1, T2, flags, st));  // H22 <- Si
-  // T2 [n1 x n2] = C * Si^T   (Z = C Si)
-  IC_TRY(gemm_tn(n1, n2, n2, 1.f, H12.hi, H12.lo, ld, H22.hi, H22.lo, ld, 0.f, nullptr, nullptr, ld2, T2.hi,
-                 T2.lo, ld2, 3, st));
-  // H11 <- Ai + Z * C^T
-  IC_TRY(gemm_tn(n1, n1, n2, 1.f, T2.hi, T2.lo, ld2, H12.hi, H12.lo, ld, 1.f, H11.hi, H11.lo, ld, H11.hi,
-                 H11.lo, ld, 3, st));
-  // H12 <- -Z ; H21 <- -Z^T
-  IC_TRY(scale_copy(T2, n1, n2, ld2, -1.f, H12, ld, st));
-  IC_TRY(transpose(T2.hi, T2.lo, n1, n2, ld2, -1.f, H21.hi, H21.lo, ld, st));
-  return IC_OK;
+  const int64_t n1 = split_point(n), n2 = n - n1;
+  IC_TRY(trsm_rec(c, X, m, ldx, off, n1));
+  // X2 -= X1 * L21^T
+  IC_TRY(gemm3(c, m, n2, n1, -1.f, X, ldx, c.H.at(off + n1, off, c.ld), c.ld, 1.f, X.at(0, n1, ldx), ldx, true));
+  return trsm_rec(c, X.at(0, n1, ldx), m, ldx, off + n1, n2);
+}
+
+// lower Cholesky factor of the diagonal block at off (size n), in place
+int chol_rec(const Ctx& c, int64_t off, int64_t n) {
+  if (n <= BASE) {
+    Pair A = c.H.at(off, off, c.ld), S = c.slot(off);
+    chol_base_kernel<<<1, 512, BASE_SMEM, c.st>>>(A.hi, A.lo, (int)n, c.ld, S.hi, S.lo, c.flags);
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
+  const int64_t n1 = split_point(n), n2 = n - n1;
+  IC_TRY(chol_rec(c, off, n1));
+  Pair A21 = c.H.at(off + n1, off, c.ld);
+  IC_TRY(trsm_rec(c, A21, n2, c.ld, off, n1));  // L21 = A21 L11^-T
+  IC_TRY(gemm3(c, n2, n2, n1, -1.f, A21, c.ld, A21, c.ld, 1.f, c.H.at(off + n1, off + n1, c.ld), c.ld, true));
+  return chol_rec(c, off + n1, n2);
+}
+
+// U block at (off, off) of size n <- L^-T (upper triangular)
+int invt_rec(const Ctx& c, int64_t off, int64_t n) {
+  if (n <= BASE) {
+    Pair S = c.slot(off), Ub = c.U.at(off, off, c.ld);
+    dim3 grid((unsigned)cdiv(n, 32), (unsigned)cdiv(n, 32));
+    transpose_kernel<<<grid, dim3(32, 8), 0, c.st>>>(S.hi, S.lo, n, n, BASE, 1.f, Ub.hi, Ub.lo, c.ld);
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
+  const int64_t n1 = split_point(n), n2 = n - n1;
+  IC_TRY(invt_rec(c, off, n1));
+  IC_TRY(invt_rec(c, off + n1, n2));
+  Pair U12 = c.U.at(off, off + n1, c.ld);
+  // U12 = (-U11 L21^T) L22^-T
+  IC_TRY(gemm3(c, n1, n2, n1, -1.f, c.U.at(off, off, c.ld), c.ld, c.H.at(off + n1, off, c.ld), c.ld, 0.f, U12,
+               c.ld, false));
+  return trsm_rec(c, U12, n1, c.ld, off + n1, n2);
+}
+
+size_t ws_layout(int64_t n, int64_t ld, Ctx* c, void* base, size_t cap) {
+  Carver cv(base, cap);
+  const size_t usz = (size_t)n * ld;
+  const size_t nslot = (size_t)cdiv(n, BASE);
+  Pair U{cv.take<float>(usz), cv.take<float>(usz)};
+  Pair L{cv.take<float>(nslot * BASE * BASE), cv.take<float>(nslot * BASE * BASE)};
+  Pair T{cv.take<float>((size_t)n * BASE), cv.take<float>((size_t)n * BASE)};
+  if (c) {
+    c->U = U;
+    c->Linv = L;
+    c->T = T;
+  }
+  return cv.off + 1024;
 }
 
 }  // namespace
 
-size_t spd_inverse_ws(int64_t n) {
-  const int64_t n1 = split_point(n);
-  const int64_t n2 = std::max<int64_t>(n - n1, 1);
-  const size_t per = (size_t)n1 * (size_t)std::max<int64_t>(round4(n2), 4) * 4;
-  return 4 * (per + 256) + 1024;
-}
+size_t spd_inverse_ws(int64_t n) { return ws_layout(n, (n + 3) & ~int64_t(3), nullptr, nullptr, 0); }
 
 int transpose(const float* in_hi, const float* in_lo, int64_t rows, int64_t cols, int64_t ldi, float alpha,
               float* out_hi, float* out_lo, int64_t ldo, cudaStream_t st) {
@@ -217,20 +270,31 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   if (ldh % 4) return fail(IC_ERR_INVALID, "spd_inverse: ld must be a multiple of 4");
   unsigned* flags = device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
-  if (ws_bytes < spd_inverse_ws(n)) return fail(IC_ERR_WORKSPACE, "spd_inverse: workspace too small");
+  Ctx c{};
+  c.H = Pair{h_hi, h_lo};
+  c.ld = ldh;
+  c.flags = flags;
+  c.st = st;
+  // the workspace holds U with the caller's leading dimension
+  const size_t need = ws_layout(n, ldh, &c, ws, ws_bytes);
+  if (ws_bytes < need) return fail(IC_ERR_WORKSPACE, "spd_inverse: workspace too small (%zu < %zu)", ws_bytes, need);
+  static bool attr = false;
+  if (!attr) {
+    IC_CUDA(cudaFuncSetAttribute(chol_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BASE_SMEM));
+    attr = true;
+  }
   unsigned prev = 0;
   IC_TRY(read_and_clear_flags(&prev, st));
   if (damping >= 0.f) {
     damp_kernel<<<1, 1024, 0, st>>>(h_hi, h_lo, n, ldh, damping);
     IC_CHECK_LAUNCH();
   }
-  const int64_t n1 = split_point(n);
-  const int64_t n2 = std::max<int64_t>(n - n1, 1);
-  Carver cv(ws, ws_bytes);
-  const size_t per = (size_t)n1 * (size_t)std::max<int64_t>(round4(n2), 4);
-  Pair T1{cv.take<float>(per), cv.take<float>(per)};
-  Pair T2{cv.take<float>(per), cv.take<float>(per)};
-  IC_TRY(inv_rec(Pair{h_hi, h_lo}, n, ldh, T1, T2, flags, st));
+  IC_CUDA(cudaMemsetAsync(c.U.hi, 0, (size_t)n * ldh * 4, st));
+  IC_CUDA(cudaMemsetAsync(c.U.lo, 0, (size_t)n * ldh * 4, st));
+  IC_TRY(chol_rec(c, 0, n));
+  IC_TRY(invt_rec(c, 0, n));
+  // H^-1 = U U^T
+  IC_TRY(gemm3(c, n, n, n, 1.f, c.U, ldh, c.U, ldh, 0.f, c.H, ldh, false));
   unsigned f = 0;
   IC_TRY(read_and_clear_flags(&f, st));
   if (f & DEV_TIMEOUT) return fail(IC_ERR_TIMEOUT, "spd_inverse: a tensor-core wait timed out");

@@ -56,8 +56,9 @@ def test_gemm_tn(m, n, k, passes):
                              nat.stream_ptr(D.device)))
     torch.cuda.synchronize()
     ref = 2.0 * Cm.double() - 0.5 * (A.double() @ Bm.double().T)
-    err = (D.double() - ref).abs().max().item() / (np.sqrt(k) + 1)
-    assert err < (2e-5 if passes == 3 else 3e-3), err
+    scale = 2.0 * Cm.double().abs() + 0.5 * (A.double().abs() @ Bm.double().abs().T)
+    err = ((D.double() - ref).abs() / scale).max().item()
+    assert err < (1e-5 if passes == 3 else 2e-3), err
 
 
 def test_gemm_pair_output():
@@ -131,8 +132,7 @@ def test_rtn_api(golden, name):
 def test_rtn_fused(golden, name):
     c = C.RTN_CASES[name]
     W = C.rtn_weight(c)
-    out = B.rtn_quantize_fused(cu(W).half() if c.get("dist") != "heavy" else cu(W), c["rot"], c["bits"], c["asym"],
-                               c["ratios"])
+    out = B.rtn_quantize_fused(cu(W), c["rot"], c["bits"], c["asym"], c["ratios"])
     assert np.array_equal(np_(out["scales"]), golden[name + "/scales"])
     if c["asym"]:
         assert np.array_equal(np_(out["zero_points"]), golden[name + "/zp"])
@@ -176,7 +176,9 @@ def test_spd_inverse(n, ns):
     assert path == "cholesky"
     out = np_(out).astype(np.float64)
     rel = np.abs(out - ref).max() / np.abs(ref).max()
-    assert rel < 2e-3 * max(1.0, np.linalg.cond(Hd) / 1e4), rel
+    lapack, _ = R.invert_hessian(R.damp(H, 0.01))  # fp32 LAPACK, the reference's own arithmetic
+    rel_lapack = np.abs(lapack - ref).max() / np.abs(ref).max()
+    assert rel < max(8 * rel_lapack, 1e-5), (rel, rel_lapack)
     assert np.abs(out - out.T).max() <= 1e-6 * np.abs(out).max()
 
 
