@@ -121,31 +121,42 @@ struct Cfg {
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (PASSES == 3 ? 2 : 1);
   static constexpr int STAGES = 196608 / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  // 3xTF32: K is accumulated in chunks of CHUNK k-tiles into two alternating
+  // TMEM accumulators; the epilogue adds the chunks in fp32 registers with
+  // round-to-nearest.  The tensor core's own fp32 accumulation truncates, and
+  // over a long K its bias adds up; chunking bounds that to CHUNK*32 terms.
+  static constexpr bool CHUNKED = PASSES == 3;
+  static constexpr int CHUNK = 2;
+  static constexpr int NACC = CHUNKED ? 2 : 1;
+  static constexpr int TMEM_COLS = NACC * BN;
 };
 
 template <int BN, int PASSES>
 __global__ void __launch_bounds__(256, 1)
-    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA_hi,
-                   const __grid_constant__ CUtensorMap tmA_lo,
-                   const __grid_constant__ CUtensorMap tmB_hi,
-                   const __grid_constant__ CUtensorMap tmB_lo, const GemmArgs args) {
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA_hi, const __grid_constant__ CUtensorMap tmA_lo,
+                   const __grid_constant__ CUtensorMap tmB_hi, const __grid_constant__ CUtensorMap tmB_lo,
+                   const GemmArgs args) {
   using C = Cfg<BN, PASSES>;
   constexpr int STAGES = C::STAGES;
+  constexpr int CH = C::CHUNKED ? C::CHUNK : (1 << 30);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+  // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], then the TMEM slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM;
   const int n0 = blockIdx.x * BN;
   const int ktiles = (args.k + BK - 1) / BK;
+  const int nchunks = C::CHUNKED ? (ktiles + CH - 1) / CH : (ktiles > 0 ? 1 : 0);
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
-  const uint32_t acc_bar = smem_u32(bars + 2 * STAGES);
+  auto accf_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + b); };
+  auto acce_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + 2 + b); };
   auto a_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES); };
   auto b_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES); };
   auto a_lo = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES); };
@@ -156,13 +167,15 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    mbar_init(acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 4);  // one arrival per epilogue warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 2) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(BN));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -188,66 +201,93 @@ __global__ void __launch_bounds__(256, 1)
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                ((uint32_t)(BM >> 4) << 24);
-    for (int kt = 0; kt < ktiles; ++kt) {
+    bool ok = true;
+    for (int kt = 0; kt < ktiles && ok; ++kt) {
+      const int chunk = C::CHUNKED ? kt / CH : 0;
+      const int b = chunk & 1;
+      const bool first_in_chunk = C::CHUNKED ? (kt % CH == 0) : (kt == 0);
+      if (C::CHUNKED && first_in_chunk && chunk >= 2 &&
+          !mbar_wait(acce_bar(b), ((chunk >> 1) & 1) ^ 1, args.flags)) {
+        ok = false;
+        break;
+      }
       const int s = kt % STAGES;
       const uint32_t ph = (kt / STAGES) & 1;
-      if (!mbar_wait(full_bar(s), ph, args.flags)) break;
+      if (!mbar_wait(full_bar(s), ph, args.flags)) {
+        ok = false;
+        break;
+      }
       asm volatile("tcgen05.fence::after_thread_sync;");
+      const uint32_t acc = tmem + (uint32_t)(b * BN);
 #pragma unroll
       for (int kk = 0; kk < BK / 8; ++kk) {
         const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
         const uint64_t ah = sdesc(a_hi(s) + off), bh = sdesc(b_hi(s) + off);
-        mma_tf32(tmem, ah, bh, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+        mma_tf32(acc, ah, bh, idesc, (first_in_chunk && kk == 0) ? 0u : 1u);
         if (PASSES == 3) {
           const uint64_t al = sdesc(a_lo(s) + off), bl = sdesc(b_lo(s) + off);
-          mma_tf32(tmem, ah, bl, idesc, 1u);
-          mma_tf32(tmem, al, bh, idesc, 1u);
+          mma_tf32(acc, ah, bl, idesc, 1u);
+          mma_tf32(acc, al, bh, idesc, 1u);
         }
       }
       mma_commit(empty_bar(s));
+      const bool last_in_chunk = C::CHUNKED ? (kt % CH == CH - 1 || kt == ktiles - 1) : (kt == ktiles - 1);
+      if (last_in_chunk) mma_commit(accf_bar(b));
     }
-    if (ktiles > 0) mma_commit(acc_bar);
   } else if (warp >= 4) {
     // ---------------- epilogue ----------------
     const int wq = warp - 4;  // TMEM lane quarter this warp may access
     const int row = m0 + wq * 32 + lane;
-    const bool have_acc = ktiles > 0 && mbar_wait(acc_bar, 0, args.flags);
-    asm volatile("tcgen05.fence::after_thread_sync;");
-    const bool row_ok = row < args.m;
-#pragma unroll 1
-    for (int cc = 0; cc < BN / 32; ++cc) {
-      uint32_t r[32];
-      if (have_acc) {
-        const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(cc * 32);
+    float sum[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) sum[j] = 0.f;
+    bool alive = true;
+    for (int c = 0; c < nchunks && alive; ++c) {
+      const int b = c & 1;
+      if (!mbar_wait(accf_bar(b), (c >> 1) & 1, args.flags)) {
+        alive = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(b * BN + cc * 32);
         IC_TMEM_LD32(taddr, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
+        for (int j = 0; j < 32; ++j) sum[cc * 32 + j] = __fadd_rn(sum[cc * 32 + j], __uint_as_float(r[j]));
       }
-      const int col0 = n0 + cc * 32;
-      if (!row_ok || col0 >= args.n) continue;
-      const float* crow_hi = args.c_hi ? args.c_hi + (long long)row * args.ldc + col0 : nullptr;
-      const float* crow_lo = args.c_lo ? args.c_lo + (long long)row * args.ldc + col0 : nullptr;
-      float* drow_hi = args.d_hi + (long long)row * args.ldd + col0;
-      float* drow_lo = args.d_lo ? args.d_lo + (long long)row * args.ldd + col0 : nullptr;
+      if (C::CHUNKED) {
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce_bar(b)) : "memory");
+      }
+    }
+    if (row < args.m) {
+      const float* crow_hi = args.c_hi ? args.c_hi + (long long)row * args.ldc : nullptr;
+      const float* crow_lo = args.c_lo ? args.c_lo + (long long)row * args.ldc : nullptr;
+      float* drow_hi = args.d_hi + (long long)row * args.ldd;
+      float* drow_lo = args.d_lo ? args.d_lo + (long long)row * args.ldd : nullptr;
       const bool read_c = args.beta != 0.f && crow_hi != nullptr;
-      if (args.vec && col0 + 32 <= args.n) {
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float v[4];
+      for (int j4 = 0; j4 < BN / 4; ++j4) {
+        const int col = n0 + j4 * 4;
+        if (col >= args.n) break;
+        float v[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) v[t] = args.alpha * __uint_as_float(r[j4 * 4 + t]);
+        for (int t = 0; t < 4; ++t) v[t] = args.alpha * sum[j4 * 4 + t];
+        if (args.vec && col + 4 <= args.n) {
           if (read_c) {
-            float4 c = reinterpret_cast<const float4*>(crow_hi)[j4];
+            float4 cv = *reinterpret_cast<const float4*>(crow_hi + col);
             if (crow_lo) {
-              const float4 cl = reinterpret_cast<const float4*>(crow_lo)[j4];
-              c.x += cl.x; c.y += cl.y; c.z += cl.z; c.w += cl.w;
+              const float4 cl = *reinterpret_cast<const float4*>(crow_lo + col);
+              cv.x += cl.x; cv.y += cl.y; cv.z += cl.z; cv.w += cl.w;
             }
-            v[0] = fmaf(args.beta, c.x, v[0]);
-            v[1] = fmaf(args.beta, c.y, v[1]);
-            v[2] = fmaf(args.beta, c.z, v[2]);
-            v[3] = fmaf(args.beta, c.w, v[3]);
+            v[0] = fmaf(args.beta, cv.x, v[0]);
+            v[1] = fmaf(args.beta, cv.y, v[1]);
+            v[2] = fmaf(args.beta, cv.z, v[2]);
+            v[3] = fmaf(args.beta, cv.w, v[3]);
           }
           if (drow_lo) {
             float4 h, l;
@@ -255,29 +295,29 @@ __global__ void __launch_bounds__(256, 1)
             split_tf32(v[1], h.y, l.y);
             split_tf32(v[2], h.z, l.z);
             split_tf32(v[3], h.w, l.w);
-            reinterpret_cast<float4*>(drow_hi)[j4] = h;
-            reinterpret_cast<float4*>(drow_lo)[j4] = l;
+            *reinterpret_cast<float4*>(drow_hi + col) = h;
+            *reinterpret_cast<float4*>(drow_lo + col) = l;
           } else {
-            reinterpret_cast<float4*>(drow_hi)[j4] = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4*>(drow_hi + col) = make_float4(v[0], v[1], v[2], v[3]);
           }
-        }
-      } else {
+        } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (col0 + j >= args.n) continue;
-          float v = args.alpha * __uint_as_float(r[j]);
-          if (read_c) {
-            float c = crow_hi[j];
-            if (crow_lo) c += crow_lo[j];
-            v = fmaf(args.beta, c, v);
-          }
-          if (drow_lo) {
-            float h, l;
-            split_tf32(v, h, l);
-            drow_hi[j] = h;
-            drow_lo[j] = l;
-          } else {
-            drow_hi[j] = v;
+          for (int t = 0; t < 4; ++t) {
+            if (col + t >= args.n) break;
+            float x = v[t];
+            if (read_c) {
+              float cv = crow_hi[col + t];
+              if (crow_lo) cv += crow_lo[col + t];
+              x = fmaf(args.beta, cv, x);
+            }
+            if (drow_lo) {
+              float h, l;
+              split_tf32(x, h, l);
+              drow_hi[col + t] = h;
+              drow_lo[col + t] = l;
+            } else {
+              drow_hi[col + t] = x;
+            }
           }
         }
       }
@@ -287,7 +327,7 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   if (warp == 2) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
 }
 
@@ -375,8 +415,8 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
     return launch<128, 3>(ah, al, bh, bl, a, st);
   }
   IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
-  IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 256));
-  return launch<256, 1>(ah, ah, bh, bh, a, st);
+  IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 128));
+  return launch<128, 1>(ah, ah, bh, bh, a, st);
 }
 
 }  // namespace ic
