@@ -42,6 +42,9 @@ const char* ic_version(void);
 const char* ic_last_error(void);
 /* IC_OK if the current device is sm_100 (B200 class); IC_ERR_UNSUPPORTED otherwise */
 int ic_device_check(void);
+/* Number of kernels this library has launched in the process (all devices);
+ * the benchmark uses it to count its own launches inside a timed region. */
+unsigned long long ic_launch_count(void);
 /* Reads and clears the device status word (bit0 timeout, bit1 not-PD,
  * bit2 INT4 range).  Synchronises `stream`. */
 int ic_device_status(unsigned* flags_out, void* stream);

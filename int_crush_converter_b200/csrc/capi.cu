@@ -1,6 +1,7 @@
 // Library-wide plumbing: error strings, the per-device status word, version.
 #include <stdarg.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -13,7 +14,10 @@ namespace {
 thread_local std::string g_err;
 std::mutex g_flag_mu;
 unsigned* g_flags[64] = {nullptr};
+std::atomic<unsigned long long> g_launches{0};
 }  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int fail(int code, const char* fmt, ...) {
   char buf[1024];
@@ -72,3 +76,5 @@ extern "C" int ic_device_status(unsigned* flags_out, void* stream) {
   if (flags_out) *flags_out = f;
   return s;
 }
+
+extern "C" unsigned long long ic_launch_count(void) { return ic::g_launches.load(); }

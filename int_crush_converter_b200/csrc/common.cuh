@@ -30,8 +30,11 @@ int fail(int code, const char* fmt, ...);
                         cudaGetErrorString(_e), __FILE__, __LINE__);           \
   } while (0)
 
+void count_launch();
+
 #define IC_CHECK_LAUNCH()                                                      \
   do {                                                                         \
+    ::ic::count_launch();                                                      \
     cudaError_t _e = cudaGetLastError();                                       \
     if (_e != cudaSuccess)                                                     \
       return ::ic::fail(IC_ERR_CUDA, "kernel launch failed: %s (%s:%d)",       \
