@@ -1,0 +1,367 @@
+"""Benchmark: GPTQ-INT4 rot-256 Mparams quantized/s (BASELINE.json metric, config 3).
+
+A "step" quantizes one synthetic DiT linear set -- qkv [12288,4096],
+proj [4096,4096], mlp_up [16384,4096], mlp_down [4096,16384] (201.3 M params)
+-- through the whole per-layer hot path: rotate W (fp16 in HBM) and its
+Hessian, row scales / zero-points, damping, tensor-core inverse, GPTQ column
+loop with the lazy tensor-core update, INT4 packing and the verify statistics.
+Each layer's Hessian is H = X^T X / 8192 with X rows N(0, diag(s^2)),
+s ~ LogNormal(0, 1) (seeded, generated on the device before timing).  Sets are
+resident in HBM (~1.7 GB each, far larger than L2) and cycled, so no step
+reads a warm input.
+
+Modes:
+  python bench.py [--gpus N --steps K --warmup W]      B200 path (one process per GPU)
+  python bench.py --impl reference ...                 the reference's CPU algorithm (oracle
+                                                       restatement) on the host cores
+Multi-GPU: each rank quantizes its own sets (layers are independent, weak
+scaling); timing is the max over ranks of the device-event time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# (name, out_features, in_features) of one DiT linear set (config 3)
+LAYERS = [("qkv", 12288, 4096), ("proj", 4096, 4096), ("mlp_up", 16384, 4096), ("mlp_down", 4096, 16384)]
+PARAMS_PER_SET = sum(m * n for _, m, n in LAYERS)
+N_SAMPLES = 8192
+ROT, BLOCK, DAMP = 256, 128, 0.01
+METRIC = "GPTQ-INT4 rot256 Mparams quantized/s"
+CONFIG = {"workload": "config 3: GPTQ INT4 rot256, block 128, damping 0.01; one step = one synthetic DiT linear "
+                      "set qkv[12288,4096] proj[4096,4096] mlp_up[16384,4096] mlp_down[4096,16384] (201.3M params), "
+                      "fp16 W ~ N(0,0.02^2), H = X^T X/8192 with X rows N(0, diag(s^2)), s ~ LogNormal(0,1)",
+          "rot_size": ROT, "block_size": BLOCK, "damping": DAMP, "int_bits": 4,
+          "l2": "inputs larger than L2 (each set ~1.7 GB, sets cycled)"}
+
+
+def make_set(seed: int, dev: torch.device):
+    """One synthetic linear set on the device: fp16 W ~ N(0, 0.02^2), H = X^T X / 8192."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = []
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for li, (name, m, n) in enumerate(LAYERS):
+        W = (torch.randn(m, n, generator=g, device=dev) * 0.02).half()
+        s = torch.exp(torch.randn(n, generator=g, device=dev))  # LogNormal(0, 1) channel scales
+        H = torch.zeros(n, n, device=dev)
+        for c0 in range(0, N_SAMPLES, 2048):  # X in chunks to bound the temporary
+            X = torch.randn(min(2048, N_SAMPLES - c0), n, generator=g, device=dev) * s
+            H.addmm_(X.T, X)
+            del X
+        H.div_(N_SAMPLES)
+        H = 0.5 * (H + H.T)
+        out.append((name, W, H))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU (oracle) arm
+def cpu_sample_seconds(reps: int = 1):
+    """Time the reference algorithm (oracle/cpu_ref.py, numpy + LAPACK on all host
+    cores) on the proj layer [4096, 4096] of a seeded set; returns (seconds/rep, params)."""
+    import numpy as np
+    from oracle import cpu_ref as R
+    from tests.golden import inputs as gi
+    name, m, n = LAYERS[1]
+    W = gi.weight_outlier_cols(1234, m, n, frac=0.0005, mult=1.0)
+    H = gi.hessian_lognormal(4321, n, N_SAMPLES)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        Wr = R.rotate_weights(W, ROT)
+        Hr = R.rotate_hessian(H, ROT)
+        r = R.gptq_quantize_layer(Wr, Hr, BLOCK, DAMP, 4)
+        R.pack_int4(r["quantized_W"])
+        ts.append(time.perf_counter() - t0)
+    del np
+    return ts, m * n
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_sample_seconds(1)
+    ts, params = cpu_sample_seconds(args.steps)
+    total = sum(ts)
+    val = params * len(ts) / total / 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "Mparams/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(ts), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(CONFIG, parallelism="host cores"),
+        "cpu_baseline": {"value": round(val, 4), "unit": "Mparams/s", "cores": cpu_cores(), "kind": "port",
+                         "sample": "one proj layer [4096,4096] per step through oracle/cpu_ref.py (numpy + "
+                                   "LAPACK, the reference's algorithm): rotate W and H, damped Cholesky inverse, "
+                                   "GPTQ column loop, pack"},
+        "e2e": {"value": round(val, 4), "unit": "Mparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- B200 arm
+def dominant_gemm_tflops(dev: torch.device, n: int = 16384, reps: int = 3) -> tuple[float, float]:
+    """The dominant kernel (3xTF32 tcgen05 GEMM) at the largest shape a step runs
+    (the n x n x n product H^-1 = U U^T of the mlp_down inverse), timed with CUDA
+    events on the launching stream.  Returns (algorithmic TFLOP/s, ms per launch)."""
+    from int_crush_converter_b200 import _native as nat
+    lib = nat.load()
+    g = torch.Generator(device=dev).manual_seed(7)
+    hi = torch.randn(n, n, generator=g, device=dev)
+    lo = torch.zeros_like(hi)
+    out_hi = torch.empty_like(hi)
+    out_lo = torch.empty_like(hi)
+    st = nat.stream_ptr(dev)
+
+    def go():
+        nat.check(lib.ic_gemm_tn(n, n, n, 1.0, hi.data_ptr(), lo.data_ptr(), n, hi.data_ptr(), lo.data_ptr(), n,
+                                 0.0, None, None, n, out_hi.data_ptr(), out_lo.data_ptr(), n, 3, st), "gemm")
+    go()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        go()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    del hi, lo, out_hi, out_lo
+    return 2.0 * n ** 3 / (ms * 1e-3) / 1e12, ms
+
+
+def run_device(args, rank: int, world: int) -> None:
+    import int_crush_converter_b200 as B
+    from int_crush_converter_b200 import _native as nat
+
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    nat.require_device(dev)
+    n_sets = max(1, min(args.sets, args.steps))
+    sets = [make_set(1000 * rank + i, dev) for i in range(n_sets)]
+    ws = B.LayerWorkspace()
+    outs = {}
+    for name, m, n in LAYERS:
+        outs[name] = dict(packed=torch.empty(m, n // 2, dtype=torch.uint8, device=dev),
+                          scales=torch.empty(m, 1, dtype=torch.float16, device=dev),
+                          zero_points=torch.empty(m, 1, dtype=torch.int8, device=dev),
+                          stats=torch.empty(2, dtype=torch.float64, device=dev))
+
+    def step(i):
+        for name, W, H in sets[i % n_sets]:
+            B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, out=outs[name], ws=ws)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    lib = nat.load()
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = int(cvd.split(",")[local]) if cvd and cvd.split(",")[local].strip().isdigit() else local
+    with ClockSampler(phys) as clk:
+        l0 = lib.ic_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for i in range(args.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        launches = lib.ic_launch_count() - l0
+    if world > 1:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = PARAMS_PER_SET * args.steps * world / (ms_max * 1e-3) / 1e6
+    del sets
+    torch.cuda.empty_cache()
+
+    e2e = run_e2e(args, dev, ws, world)
+    if rank != 0:
+        return
+    achieved, gemm_ms = dominant_gemm_tflops(dev)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    peak = bf16 / 2.0 / 3.0  # TF32 runs at half the bf16 rate; 3xTF32 issues three products
+    cpu_ts, cpu_params = cpu_sample_seconds(1)
+    cpu_val = cpu_params / cpu_ts[0] / 1e6
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic",
+        "config": dict(CONFIG, parallelism=f"layer sets sharded over {world} GPU(s), no collective"),
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": TRAFFIC_BYTES,
+                     "kernel": "gemm_tn_kernel<128,3> (3xTF32), 16384^3 product of the mlp_down inverse, "
+                               f"{gemm_ms:.2f} ms/launch",
+                     "peak_basis": ("measured bf16 burst / 2 (TF32 rate) / 3 (3xTF32 products), of measured"
+                                    if "bf16_tflops" in peaks else "fallback 1.59 PF bf16 / 2 / 3, of fallback")},
+        "cpu_baseline": {"value": round(cpu_val, 4), "unit": "Mparams/s", "cores": cpu_cores(), "kind": "port",
+                         "sample": "one proj layer [4096,4096] through oracle/cpu_ref.py (numpy + LAPACK)"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# dram bytes (read + write) of one 16384^3 3xTF32 GEMM launch from the ncu capture summarised in
+# profiles/gemm_tn_3xtf32_16384.md (null until captured)
+TRAFFIC_BYTES = None
+
+
+def run_e2e(args, dev: torch.device, ws, world: int) -> dict:
+    """Same metric through the public API with HOST buffers: every step copies one
+    set's fp16 weights and fp32 Hessians from pinned host memory, quantizes, and
+    reads back the packed codes, scales and zero-points."""
+    import int_crush_converter_b200 as B
+    host = []
+    for name, W, H in make_set(99, dev):
+        host.append((name, W.cpu().pin_memory(), H.cpu().pin_memory()))
+    torch.cuda.empty_cache()
+    res = {}
+    for name, m, n in LAYERS:
+        res[name] = (torch.empty(m, n // 2, dtype=torch.uint8).pin_memory(),
+                     torch.empty(m, 1, dtype=torch.float16).pin_memory(),
+                     torch.empty(m, 1, dtype=torch.int8).pin_memory())
+    h2d = sum(W.numel() * 2 + H.numel() * 4 for _, W, H in host)
+    d2h = sum(p.numel() + s.numel() * 2 + z.numel() for p, s, z in res.values())
+    steps = max(1, min(args.steps, args.e2e_steps))
+
+    def step():
+        for name, Wh, Hh in host:
+            W = Wh.to(dev, non_blocking=True)
+            H = Hh.to(dev, non_blocking=True)
+            o = B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, ws=ws)
+            p, s, z = res[name]
+            p.copy_(o["packed"], non_blocking=True)
+            s.copy_(o["scales"], non_blocking=True)
+            z.copy_(o["zero_points"], non_blocking=True)
+
+    step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    val = PARAMS_PER_SET * steps * world / (float(t.item()) * 1e-3) / 1e6
+    return {"value": round(val, 3), "unit": "Mparams/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "steps": steps, "api": "int_crush_converter_b200.quantize_gptq_layer (C ABI ic_gptq_layer)"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl")
+    try:
+        run_device(args, rank, world)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
