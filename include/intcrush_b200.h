@@ -159,6 +159,24 @@ int ic_gptq_run(float* W_work, int64_t ldw, const float* W0, int64_t ldw0, int64
                 float* row_maxerr, int gemm_passes, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* Same as ic_gptq_run, for callers that cannot allocate device memory (their
+ * device memory is owned and capped by another allocator, or an allocation is
+ * not acceptable on their latency-critical path).  No counterpart in the
+ * reference (the reference allocates with torch).  Takes no workspace: its
+ * scratch is a static device array of IC_NOALLOC_SCRATCH_BYTES per GPU that
+ * lives until the process exits; shapes whose ic_gptq_workspace_size exceeds
+ * it are rejected with IC_ERR_UNSUPPORTED.  Calls no cudaMalloc/cudaFree.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture).  All calls share the array, so calls that overlap on the
+ * GPU race; serialise them. */
+#define IC_NOALLOC_SCRATCH_BYTES (32u << 20)
+int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw0, int64_t M,
+                        int64_t N, const float* hinv_hi, const float* hinv_lo, int64_t ldh,
+                        int block_size, int superblock, const float* scale, const float* zp,
+                        int qmin, int qmax, int8_t* codes, int64_t ldq, uint8_t* packed,
+                        int64_t ldp, double* row_sqerr, float* row_maxerr, int gemm_passes,
+                        void* stream);
+
 /* One whole GPTQ layer as pipeline.py:547-559 + 702-809 + 919-931 + 1010-1013
  * run it: rotate W (fp16/bf16/fp32) and H, row params, damping, inverse,
  * column loop, pack, verify statistics.  H fp32 [N_in, N_in] (already in the

@@ -42,6 +42,14 @@ unsigned* device_flags() {
   return g_flags[dev];
 }
 
+// Lets a caller that must not allocate supply the status word of `dev` from
+// its own storage; has no effect when the word already exists.
+void register_device_flags(int dev, unsigned* p) {
+  if (dev < 0 || dev >= 64 || !p) return;
+  std::lock_guard<std::mutex> lk(g_flag_mu);
+  if (!g_flags[dev]) g_flags[dev] = p;
+}
+
 int read_and_clear_flags(unsigned* out, cudaStream_t st) {
   unsigned* f = device_flags();
   if (!f) return fail(IC_ERR_CUDA, "device status word unavailable");

@@ -20,6 +20,7 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
                 size_t ws_bytes, cudaStream_t st);
 size_t spd_inverse_ws(int64_t n);
 int read_and_clear_flags(unsigned* out, cudaStream_t st);
+void register_device_flags(int dev, unsigned* p);
 int finalize_stats(const double* row_sqerr, const float* row_maxerr, int64_t M, double count,
                    double* stats, cudaStream_t st);
 
