@@ -347,7 +347,14 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--gemm-only", type=int, default=0,
+                    help="time only the dominant 3xTF32 GEMM at n^3 (small profiling case)")
     args = ap.parse_args()
+    if args.gemm_only:
+        dev = torch.device("cuda", 0)
+        tf, ms = dominant_gemm_tflops(dev, n=args.gemm_only, reps=2)
+        print(json.dumps({"gemm_n": args.gemm_only, "tflops": round(tf, 2), "ms": round(ms, 3)}))
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
