@@ -32,6 +32,9 @@ struct GemmArgs {
   long long ldd;
   unsigned* flags;
   int vec;  // C/D rows 16-byte aligned: vectorised epilogue
+  int tri;  // bit 0: only output tiles on/below the diagonal (n0 <= m0);
+            // bit 1: A rows are zero left of their own index (upper triangular
+            //        A), so the K loop starts at the tile's first row m0
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -150,7 +153,9 @@ __global__ void __launch_bounds__(256, 1)
   const int lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM;
   const int n0 = blockIdx.x * BN;
-  const int ktiles = (args.k + BK - 1) / BK;
+  if ((args.tri & 1) && n0 > m0) return;  // strictly-upper tile of a symmetric/lower result
+  const int kbase = (args.tri & 2) ? min(m0, args.k) : 0;
+  const int ktiles = (args.k - kbase + BK - 1) / BK;
   const int nchunks = C::CHUNKED ? (ktiles + CH - 1) / CH : (ktiles > 0 ? 1 : 0);
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
@@ -190,11 +195,12 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t ph = (kt / STAGES) & 1;
       if (kt >= STAGES && !mbar_wait(empty_bar(s), ph ^ 1, args.flags)) break;
       mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
-      tma_load_2d(a_hi(s), &tmA_hi, kt * BK, m0, full_bar(s));
-      tma_load_2d(b_hi(s), &tmB_hi, kt * BK, n0, full_bar(s));
+      const int kx = kbase + kt * BK;
+      tma_load_2d(a_hi(s), &tmA_hi, kx, m0, full_bar(s));
+      tma_load_2d(b_hi(s), &tmB_hi, kx, n0, full_bar(s));
       if (PASSES == 3) {
-        tma_load_2d(a_lo(s), &tmA_lo, kt * BK, m0, full_bar(s));
-        tma_load_2d(b_lo(s), &tmB_lo, kt * BK, n0, full_bar(s));
+        tma_load_2d(a_lo(s), &tmA_lo, kx, m0, full_bar(s));
+        tma_load_2d(b_lo(s), &tmB_lo, kx, n0, full_bar(s));
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -390,7 +396,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
             int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
             const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
-            int64_t ldd, int passes, cudaStream_t st) {
+            int64_t ldd, int passes, cudaStream_t st, int tri) {
   if (m <= 0 || n <= 0) return IC_OK;
   if (passes != 1 && passes != 3) return fail(IC_ERR_INVALID, "gemm: passes must be 1 or 3");
   if (passes == 3 && (!a_lo || !b_lo)) return fail(IC_ERR_INVALID, "gemm: 3xTF32 needs lo parts");
@@ -404,7 +410,7 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
   unsigned* flags = device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
   GemmArgs a{(int)m, (int)n, (int)(k > 0 ? k : 0), alpha, beta, c_hi, c_lo, (long long)ldc,
-             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0};
+             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
   if (passes == 3) {

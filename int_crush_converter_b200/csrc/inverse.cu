@@ -19,8 +19,6 @@ namespace ic {
 namespace {
 
 constexpr int BASE = 128;
-constexpr int LDS = BASE + 1;
-constexpr size_t BASE_SMEM = (size_t)2 * BASE * LDS * 4;
 
 // H += lambda*I, lambda = damping * max(mean(diag H), 1e-6)  (gptq.py:118-119)
 __global__ void __launch_bounds__(1024) damp_kernel(float* hi, float* lo, int64_t n, int64_t ld, float damping) {
@@ -54,70 +52,127 @@ __device__ __forceinline__ void put_pair(float* hi, float* lo, int64_t idx, floa
 
 // Cholesky of one n x n (n <= 128) diagonal block (lower triangle read), in
 // place (lower L, upper zeroed), plus its explicit inverse Linv (lower) written
-// to the slot [128 x 128].  Inner products accumulate in fp64.
+// to the slot [128 x 128].  Blocked in 32-wide panels inside one CTA:
+//   factor the 32 x 32 diagonal block (one warp, rows in lanes, shuffles),
+//   solve the panel rows below it by substitution (one thread per row),
+//   update the trailing lower triangle (16 warps, one dot product per element);
+// then Linv by 32-blocks: the four diagonal blocks inverted in parallel (one
+// warp each, one column per lane), the off-diagonal blocks by distance from
+// the diagonal.  Padding (n < 128) is an identity block.
+constexpr int LDS = BASE + 1;
+constexpr size_t BASE_SMEM = (size_t)(2 * BASE * LDS + 3 * 32 * 33) * 4;
+
 __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, int n, int64_t ld, float* ihi,
                                                         float* ilo, unsigned* flags) {
   extern __shared__ float sm[];
-  float* a = sm;             // [BASE][LDS]  L
-  float* x = sm + BASE * LDS;  // [BASE][LDS]  Linv
+  float* a = sm;                   // [128][LDS]  A -> L
+  float* x = sm + BASE * LDS;      // [128][LDS]  Linv
+  float* tb = sm + 2 * BASE * LDS;  // [3][32][33] scratch blocks
   __shared__ int bad;
-  if (threadIdx.x == 0) bad = 0;
-  for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
-    const int i = idx / n, j = idx % n;
-    a[i * LDS + j] = i >= j ? __fadd_rn(hi[i * ld + j], lo[i * ld + j]) : 0.f;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) bad = 0;
+  for (int idx = tid; idx < BASE * BASE; idx += blockDim.x) {
+    const int i = idx >> 7, j = idx & 127;
+    float v;
+    if (i < n && j < n) v = (i >= j) ? __fadd_rn(hi[(int64_t)i * ld + j], lo[(int64_t)i * ld + j]) : 0.f;
+    else v = (i == j) ? 1.f : 0.f;
+    a[i * LDS + j] = v;
+    x[i * LDS + j] = 0.f;
   }
   __syncthreads();
-  // left-looking column Cholesky: column k computed after columns < k
-  for (int k = 0; k < n; ++k) {
-    // diagonal
-    if (threadIdx.x < 32) {
-      double s = 0.0;
-      for (int t = threadIdx.x; t < k; t += 32) s += (double)a[k * LDS + t] * a[k * LDS + t];
-      s = warp_sum_d(s);
-      if (threadIdx.x == 0) {
-        const double d = (double)a[k * LDS + k] - s;
-        if (!(d > 0.0) || !isfinite(d)) {
-          bad = 1;
-          a[k * LDS + k] = 1.f;
-        } else {
-          a[k * LDS + k] = (float)sqrt(d);
+  for (int p0 = 0; p0 < BASE; p0 += 32) {
+    // (1) 32 x 32 diagonal block, one warp: lane i holds row p0+i
+    if (warp == 0) {
+      float row[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) row[j] = (j <= lane) ? a[(p0 + lane) * LDS + p0 + j] : 0.f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        float d = __shfl_sync(0xffffffffu, row[k], k);
+        if (!(d > 0.f) || !isfinite(d)) {
+          if (lane == 0) bad = 1;
+          d = 1.f;
+        }
+        d = sqrtf(d);
+        const float l = (lane > k) ? __fdiv_rn(row[k], d) : (lane == k ? d : 0.f);
+        row[k] = l;
+#pragma unroll
+        for (int j = k + 1; j < 32; ++j) {
+          const float lj = __shfl_sync(0xffffffffu, l, j);
+          if (lane >= j) row[j] = fmaf(-l, lj, row[j]);
         }
       }
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j <= lane) a[(p0 + lane) * LDS + p0 + j] = row[j];
     }
     __syncthreads();
-    const float dkk = a[k * LDS + k];
-    // column below the diagonal: one warp per row
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int i = k + 1 + warp; i < n; i += nw) {
-      double s = 0.0;
-      for (int t = lane; t < k; t += 32) s += (double)a[i * LDS + t] * a[k * LDS + t];
-      s = warp_sum_d(s);
-      if (lane == 0) a[i * LDS + k] = (float)(((double)a[i * LDS + k] - s) / (double)dkk);
+    // (2) rows below: L21 = A21 L11^-T by forward substitution, one thread per row
+    const int r = p0 + 32 + tid;
+    if (r < BASE) {
+      float xr[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        float s = a[r * LDS + p0 + k];
+#pragma unroll
+        for (int t = 0; t < k; ++t) s = fmaf(-xr[t], a[(p0 + k) * LDS + p0 + t], s);
+        xr[k] = __fdiv_rn(s, a[(p0 + k) * LDS + p0 + k]);
+      }
+#pragma unroll
+      for (int k = 0; k < 32; ++k) a[r * LDS + p0 + k] = xr[k];
+    }
+    __syncthreads();
+    // (3) trailing update of the lower triangle: a[i][j] -= sum_t L[i][p0+t] L[j][p0+t]
+    for (int i = p0 + 32 + warp; i < BASE; i += 16) {
+      for (int j = p0 + 32 + lane; j <= i; j += 32) {
+        float s = a[i * LDS + j];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) s = fmaf(-a[i * LDS + p0 + t], a[j * LDS + p0 + t], s);
+        a[i * LDS + j] = s;
+      }
     }
     __syncthreads();
   }
-  // Linv: forward substitution, one thread per column c of the identity
-  for (int c = threadIdx.x; c < n; c += blockDim.x) {
-    for (int i = 0; i < n; ++i) {
-      if (i < c) {
-        x[i * LDS + c] = 0.f;
-        continue;
-      }
-      double s = (i == c) ? 1.0 : 0.0;
-      for (int t = c; t < i; ++t) s -= (double)a[i * LDS + t] * x[t * LDS + c];
-      x[i * LDS + c] = (float)(s / (double)a[i * LDS + i]);
+  // Linv, diagonal 32-blocks: warp w inverts block w, lane c computes column c
+  if (warp < 4) {
+    const int b0 = warp * 32, c = lane;
+    float xc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float s = (i == c) ? 1.f : 0.f;
+#pragma unroll
+      for (int t = 0; t < i; ++t) s = fmaf(-a[(b0 + i) * LDS + b0 + t], xc[t], s);
+      xc[i] = (i >= c) ? __fdiv_rn(s, a[(b0 + i) * LDS + b0 + i]) : 0.f;
     }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[(b0 + i) * LDS + b0 + c] = xc[i];
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < n * n; idx += blockDim.x) {
-    const int i = idx / n, j = idx % n;
-    put_pair(hi, lo, (int64_t)i * ld + j, i >= j ? a[i * LDS + j] : 0.f);
+  // off-diagonal blocks X[I][J] = -X[I][I] * sum_{K=J}^{I-1} L[I][K] X[K][J], by distance d = I - J
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;
+    for (int e = tid; e < nb * 1024; e += blockDim.x) {  // T = sum_K L[I][K] X[K][J]
+      const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
+      float s = 0.f;
+      for (int k = 32 * J; k < 32 * I; ++k) s = fmaf(a[(32 * I + rr) * LDS + k], x[k * LDS + 32 * J + cc], s);
+      tb[J * 32 * 33 + rr * 33 + cc] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < nb * 1024; e += blockDim.x) {  // X[I][J] = -X[I][I] T
+      const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
+      float s = 0.f;
+#pragma unroll 8
+      for (int t = 0; t <= rr; ++t) s = fmaf(x[(32 * I + rr) * LDS + 32 * I + t], tb[J * 32 * 33 + t * 33 + cc], s);
+      x[(32 * I + rr) * LDS + 32 * J + cc] = -s;
+    }
+    __syncthreads();
   }
-  for (int idx = threadIdx.x; idx < BASE * BASE; idx += blockDim.x) {
-    const int i = idx / BASE, j = idx % BASE;
-    put_pair(ihi, ilo, idx, (i < n && j < n) ? x[i * LDS + j] : 0.f);
+  for (int idx = tid; idx < BASE * BASE; idx += blockDim.x) {
+    const int i = idx >> 7, j = idx & 127;
+    if (i < n && j < n) put_pair(hi, lo, (int64_t)i * ld + j, (i >= j) ? a[i * LDS + j] : 0.f);
+    put_pair(ihi, ilo, idx, (i < n && j < n && j <= i) ? x[i * LDS + j] : 0.f);
   }
-  if (threadIdx.x == 0 && bad) atomicOr(flags, DEV_NOT_PD);
+  if (tid == 0 && bad) atomicOr(flags, DEV_NOT_PD);
 }
 
 // out = alpha * in^T on hi/lo pairs (32x32 tiles through shared memory)
@@ -146,15 +201,25 @@ __global__ void transpose_kernel(const float* __restrict__ ih, const float* __re
   }
 }
 
-// copy a [rows x cols] hi/lo block (ldi -> ldo)
-__global__ void copy_pair_kernel(const float* __restrict__ ih, const float* __restrict__ il, int64_t rows,
-                                 int64_t cols, int64_t ldi, float* __restrict__ oh, float* __restrict__ ol,
-                                 int64_t ldo) {
-  const int64_t total = rows * cols;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cols, c = i % cols;
-    oh[r * ldo + c] = ih[r * ldi + c];
-    ol[r * ldo + c] = il[r * ldi + c];
+// Fill the strictly-upper 128-tiles of a symmetric pair from its lower tiles.
+__global__ void mirror_kernel(float* __restrict__ hi, float* __restrict__ lo, int64_t n, int64_t ld) {
+  const int64_t bi = blockIdx.y, bj = blockIdx.x;  // 32 x 32 destination tile (row bi, col bj)
+  if (bj / 4 <= bi / 4) return;                      // not in a strictly-upper 128-tile
+  __shared__ float th[32][33], tl[32][33];
+  for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
+    const int64_t r = bj * 32 + dy, c = bi * 32 + threadIdx.x;  // source tile (bj, bi) in the lower part
+    if (r < n && c < n) {
+      th[dy][threadIdx.x] = hi[r * ld + c];
+      tl[dy][threadIdx.x] = lo[r * ld + c];
+    }
+  }
+  __syncthreads();
+  for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
+    const int64_t r = bi * 32 + dy, c = bj * 32 + threadIdx.x;
+    if (r < n && c < n) {
+      hi[r * ld + c] = th[threadIdx.x][dy];
+      lo[r * ld + c] = tl[threadIdx.x][dy];
+    }
   }
 }
 
@@ -178,20 +243,19 @@ struct Ctx {
 int64_t split_point(int64_t n) { return std::max<int64_t>((n / 2 / BASE) * BASE, BASE); }
 
 int gemm3(const Ctx& c, int64_t m, int64_t n, int64_t k, float alpha, Pair A, int64_t lda, Pair B, int64_t ldb,
-          float beta, Pair D, int64_t ldd, bool c_is_d) {
+          float beta, Pair D, int64_t ldd, bool c_is_d, int tri = 0) {
   return gemm_tn(m, n, k, alpha, A.hi, A.lo, lda, B.hi, B.lo, ldb, beta, c_is_d ? D.hi : nullptr,
-                 c_is_d ? D.lo : nullptr, ldd, D.hi, D.lo, ldd, 3, c.st);
+                 c_is_d ? D.lo : nullptr, ldd, D.hi, D.lo, ldd, 3, c.st, tri);
 }
 
 // X [m x n] (leading dimension ldx) <- X * L^-T, L = the factor's diagonal block at off (size n)
 int trsm_rec(const Ctx& c, Pair X, int64_t m, int64_t ldx, int64_t off, int64_t n) {
   if (m <= 0 || n <= 0) return IC_OK;
   if (n <= BASE) {
-    IC_TRY(gemm3(c, m, n, n, 1.f, X, ldx, c.slot(off), BASE, 0.f, c.T, BASE, false));
-    const int blocks = (int)std::min<int64_t>(cdiv(m * n, 256), 148 * 16);
-    copy_pair_kernel<<<blocks, 256, 0, c.st>>>(c.T.hi, c.T.lo, m, n, BASE, X.hi, X.lo, ldx);
-    IC_CHECK_LAUNCH();
-    return IC_OK;
+    // In place: with n <= 128 the product has a single column tile, so the CTA
+    // that overwrites a row block is the only one that reads it, and it has
+    // read all of it (all K) before its epilogue writes.
+    return gemm3(c, m, n, n, 1.f, X, ldx, c.slot(off), BASE, 0.f, X, ldx, false);
   }
   const int64_t n1 = split_point(n), n2 = n - n1;
   IC_TRY(trsm_rec(c, X, m, ldx, off, n1));
@@ -204,6 +268,11 @@ int trsm_rec(const Ctx& c, Pair X, int64_t m, int64_t ldx, int64_t off, int64_t 
 int chol_rec(const Ctx& c, int64_t off, int64_t n) {
   if (n <= BASE) {
     Pair A = c.H.at(off, off, c.ld), S = c.slot(off);
+    static bool attr = false;
+    if (!attr) {
+      IC_CUDA(cudaFuncSetAttribute(chol_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BASE_SMEM));
+      attr = true;
+    }
     chol_base_kernel<<<1, 512, BASE_SMEM, c.st>>>(A.hi, A.lo, (int)n, c.ld, S.hi, S.lo, c.flags);
     IC_CHECK_LAUNCH();
     return IC_OK;
@@ -212,7 +281,8 @@ int chol_rec(const Ctx& c, int64_t off, int64_t n) {
   IC_TRY(chol_rec(c, off, n1));
   Pair A21 = c.H.at(off + n1, off, c.ld);
   IC_TRY(trsm_rec(c, A21, n2, c.ld, off, n1));  // L21 = A21 L11^-T
-  IC_TRY(gemm3(c, n2, n2, n1, -1.f, A21, c.ld, A21, c.ld, 1.f, c.H.at(off + n1, off + n1, c.ld), c.ld, true));
+  // only the lower triangle of A22 is ever read again: skip its strictly-upper tiles
+  IC_TRY(gemm3(c, n2, n2, n1, -1.f, A21, c.ld, A21, c.ld, 1.f, c.H.at(off + n1, off + n1, c.ld), c.ld, true, 1));
   return chol_rec(c, off + n1, n2);
 }
 
@@ -230,8 +300,9 @@ int invt_rec(const Ctx& c, int64_t off, int64_t n) {
   IC_TRY(invt_rec(c, off + n1, n2));
   Pair U12 = c.U.at(off, off + n1, c.ld);
   // U12 = (-U11 L21^T) L22^-T
+  // U11 is upper triangular: row i of it is zero left of column i
   IC_TRY(gemm3(c, n1, n2, n1, -1.f, c.U.at(off, off, c.ld), c.ld, c.H.at(off + n1, off, c.ld), c.ld, 0.f, U12,
-               c.ld, false));
+               c.ld, false, 2));
   return trsm_rec(c, U12, n1, c.ld, off + n1, n2);
 }
 
@@ -278,11 +349,6 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   // the workspace holds U with the caller's leading dimension
   const size_t need = ws_layout(n, ldh, &c, ws, ws_bytes);
   if (ws_bytes < need) return fail(IC_ERR_WORKSPACE, "spd_inverse: workspace too small (%zu < %zu)", ws_bytes, need);
-  static bool attr = false;
-  if (!attr) {
-    IC_CUDA(cudaFuncSetAttribute(chol_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BASE_SMEM));
-    attr = true;
-  }
   unsigned prev = 0;
   IC_TRY(read_and_clear_flags(&prev, st));
   if (damping >= 0.f) {
@@ -293,8 +359,13 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   IC_CUDA(cudaMemsetAsync(c.U.lo, 0, (size_t)n * ldh * 4, st));
   IC_TRY(chol_rec(c, 0, n));
   IC_TRY(invt_rec(c, 0, n));
-  // H^-1 = U U^T
-  IC_TRY(gemm3(c, n, n, n, 1.f, c.U, ldh, c.U, ldh, 0.f, c.H, ldh, false));
+  // H^-1 = U U^T: lower tiles only, K from the tile row (U is upper triangular), then mirror
+  IC_TRY(gemm3(c, n, n, n, 1.f, c.U, ldh, c.U, ldh, 0.f, c.H, ldh, false, 3));
+  {
+    dim3 grid((unsigned)cdiv(n, 32), (unsigned)cdiv(n, 32));
+    mirror_kernel<<<grid, dim3(32, 8), 0, st>>>(h_hi, h_lo, n, ldh);
+    IC_CHECK_LAUNCH();
+  }
   unsigned f = 0;
   IC_TRY(read_and_clear_flags(&f, st));
   if (f & DEV_TIMEOUT) return fail(IC_ERR_TIMEOUT, "spd_inverse: a tensor-core wait timed out");
