@@ -50,6 +50,7 @@ struct BlockArgs {
   int64_t lde;
   double* row_sqerr;
   float* row_maxerr;
+  int vec;  // W and Hinv rows of this block are 16-byte aligned
 };
 
 template <bool LDLQ>
@@ -68,10 +69,37 @@ __global__ void __launch_bounds__(128) block_kernel(const BlockArgs a) {
   const bool rv = r < a.M;
   const int64_t rr = rv ? r : a.M - 1;  // clamp loads for the tail rows
 
-  for (int idx = threadIdx.x; idx < bc * bc; idx += blockDim.x) {
-    const int j = idx / bc, k = idx % bc;
-    const int64_t o = (a.i1 + j) * a.ldh + a.i1 + k;
-    hs[j * MAXB + k] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
+  if (a.vec && bc == MAXB) {
+    // full 128 x 128 block: float4 loads, 32 per row, 8 in flight per thread
+    const float* hb = a.h_hi + a.i1 * a.ldh + a.i1;
+    const float* lb = a.h_lo + a.i1 * a.ldh + a.i1;
+#pragma unroll 4
+    for (int it = 0; it < MAXB * MAXB / 4 / 128; it += 8) {
+      float4 hv[8], lv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = (it + u) * 128 + threadIdx.x;
+        const int j = idx >> 5, k4 = (idx & 31) << 2;
+        hv[u] = *reinterpret_cast<const float4*>(hb + j * a.ldh + k4);
+        lv[u] = *reinterpret_cast<const float4*>(lb + j * a.ldh + k4);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = (it + u) * 128 + threadIdx.x;
+        const int j = idx >> 5, k4 = (idx & 31) << 2;
+        float* d = hs + j * MAXB + k4;
+        d[0] = __fadd_rn(hv[u].x, lv[u].x);
+        d[1] = __fadd_rn(hv[u].y, lv[u].y);
+        d[2] = __fadd_rn(hv[u].z, lv[u].z);
+        d[3] = __fadd_rn(hv[u].w, lv[u].w);
+      }
+    }
+  } else {
+    for (int j = 0; j < bc; ++j)
+      for (int k = threadIdx.x; k < bc; k += blockDim.x) {
+        const int64_t o = (a.i1 + j) * a.ldh + a.i1 + k;
+        hs[j * MAXB + k] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
+      }
   }
   __syncthreads();
   if (LDLQ)
@@ -81,9 +109,21 @@ __global__ void __launch_bounds__(128) block_kernel(const BlockArgs a) {
   float w[GROUP], ev[GROUP];
   float sc[LDLQ ? GROUP : 1];
   const float* wrow = a.W + rr * a.ldw + a.i1 + cbase;
+  if (a.vec && cbase + GROUP <= bc) {
+#pragma unroll
+    for (int c4 = 0; c4 < GROUP / 4; ++c4) {
+      const float4 v = reinterpret_cast<const float4*>(wrow)[c4];
+      w[4 * c4] = v.x;
+      w[4 * c4 + 1] = v.y;
+      w[4 * c4 + 2] = v.z;
+      w[4 * c4 + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < GROUP; ++c) w[c] = (cbase + c < bc) ? wrow[c] : 0.f;
+  }
 #pragma unroll
   for (int c = 0; c < GROUP; ++c) {
-    w[c] = (cbase + c < bc) ? wrow[c] : 0.f;
     ev[c] = 0.f;
     if (LDLQ) sc[c] = (cbase + c < bc) ? fmaxf(a.scale2d[rr * a.lds + a.i1 + cbase + c], 1e-8f) : 1.f;
   }
@@ -423,6 +463,8 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
       a.qmin = (float)L.qmin; a.qmax = (float)L.qmax; a.codes = L.codes; a.ldq = L.ldq;
       a.packed = L.packed; a.ldp = L.ldp; a.e_hi = e_hi + (i1 - sb); a.e_lo = e_lo + (i1 - sb);
       a.lde = lde; a.row_sqerr = L.row_sqerr; a.row_maxerr = L.row_maxerr;
+      a.vec = ((L.ldw | L.ldh | i1) & 3) == 0 && (reinterpret_cast<uintptr_t>(L.W) & 15) == 0 &&
+              (reinterpret_cast<uintptr_t>(L.h_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(L.h_lo) & 15) == 0;
       if (L.ldlq) block_kernel<true><<<nblk, 128, BLOCK_SMEM, st>>>(a);
       else block_kernel<false><<<nblk, 128, BLOCK_SMEM, st>>>(a);
       IC_CHECK_LAUNCH();
