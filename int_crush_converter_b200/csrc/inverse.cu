@@ -71,13 +71,31 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
   __shared__ int bad;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) bad = 0;
-  for (int idx = tid; idx < BASE * BASE; idx += blockDim.x) {
-    const int i = idx >> 7, j = idx & 127;
-    float v;
-    if (i < n && j < n) v = (i >= j) ? __fadd_rn(hi[(int64_t)i * ld + j], lo[(int64_t)i * ld + j]) : 0.f;
-    else v = (i == j) ? 1.f : 0.f;
-    a[i * LDS + j] = v;
-    x[i * LDS + j] = 0.f;
+  if (n == BASE && (ld & 3) == 0 && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
+    // full block: float4 loads, 8 in flight per thread
+#pragma unroll
+    for (int it = 0; it < BASE * BASE / 4 / 512; ++it) {
+      const int idx = it * 512 + tid;
+      const int i = idx >> 5, j4 = (idx & 31) << 2;
+      const float4 h = *reinterpret_cast<const float4*>(hi + (int64_t)i * ld + j4);
+      const float4 l = *reinterpret_cast<const float4*>(lo + (int64_t)i * ld + j4);
+      float* d = a + i * LDS + j4;
+      d[0] = (i >= j4) ? __fadd_rn(h.x, l.x) : 0.f;
+      d[1] = (i >= j4 + 1) ? __fadd_rn(h.y, l.y) : 0.f;
+      d[2] = (i >= j4 + 2) ? __fadd_rn(h.z, l.z) : 0.f;
+      d[3] = (i >= j4 + 3) ? __fadd_rn(h.w, l.w) : 0.f;
+      float* dx = x + i * LDS + j4;
+      dx[0] = dx[1] = dx[2] = dx[3] = 0.f;
+    }
+  } else {
+    for (int idx = tid; idx < BASE * BASE; idx += blockDim.x) {
+      const int i = idx >> 7, j = idx & 127;
+      float v;
+      if (i < n && j < n) v = (i >= j) ? __fadd_rn(hi[(int64_t)i * ld + j], lo[(int64_t)i * ld + j]) : 0.f;
+      else v = (i == j) ? 1.f : 0.f;
+      a[i * LDS + j] = v;
+      x[i * LDS + j] = 0.f;
+    }
   }
   __syncthreads();
   for (int p0 = 0; p0 < BASE; p0 += 32) {
@@ -150,20 +168,44 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
   __syncthreads();
   // off-diagonal blocks X[I][J] = -X[I][I] * sum_{K=J}^{I-1} L[I][K] X[K][J], by distance d = I - J
   for (int d = 1; d < 4; ++d) {
-    const int nb = 4 - d;
-    for (int e = tid; e < nb * 1024; e += blockDim.x) {  // T = sum_K L[I][K] X[K][J]
-      const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
-      float s = 0.f;
-      for (int k = 32 * J; k < 32 * I; ++k) s = fmaf(a[(32 * I + rr) * LDS + k], x[k * LDS + 32 * J + cc], s);
-      tb[J * 32 * 33 + rr * 33 + cc] = s;
+    const int nb = 4 - d;  // blocks on this diagonal; each thread owns up to 6 elements (independent chains)
+    float acc[6];
+#pragma unroll
+    for (int u = 0; u < 6; ++u) acc[u] = 0.f;
+    for (int kk = 0; kk < 32 * d; ++kk) {  // T = sum_K L[I][K] X[K][J]
+#pragma unroll
+      for (int u = 0; u < 6; ++u) {
+        const int e = tid + 512 * u;
+        if (e < nb * 1024) {
+          const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
+          acc[u] = fmaf(a[(32 * I + rr) * LDS + 32 * J + kk], x[(32 * J + kk) * LDS + 32 * J + cc], acc[u]);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 6; ++u) {
+      const int e = tid + 512 * u;
+      if (e < nb * 1024) tb[(e >> 10) * 32 * 33 + ((e >> 5) & 31) * 33 + (e & 31)] = acc[u];
+      acc[u] = 0.f;
     }
     __syncthreads();
-    for (int e = tid; e < nb * 1024; e += blockDim.x) {  // X[I][J] = -X[I][I] T
-      const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
-      float s = 0.f;
-#pragma unroll 8
-      for (int t = 0; t <= rr; ++t) s = fmaf(x[(32 * I + rr) * LDS + 32 * I + t], tb[J * 32 * 33 + t * 33 + cc], s);
-      x[(32 * I + rr) * LDS + 32 * J + cc] = -s;
+    for (int t = 0; t < 32; ++t) {  // X[I][J] = -X[I][I] T  (X[I][I] lower triangular)
+#pragma unroll
+      for (int u = 0; u < 6; ++u) {
+        const int e = tid + 512 * u;
+        if (e < nb * 1024) {
+          const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
+          if (t <= rr) acc[u] = fmaf(x[(32 * I + rr) * LDS + 32 * I + t], tb[J * 32 * 33 + t * 33 + cc], acc[u]);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 6; ++u) {
+      const int e = tid + 512 * u;
+      if (e < nb * 1024) {
+        const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
+        x[(32 * I + rr) * LDS + 32 * J + cc] = -acc[u];
+      }
     }
     __syncthreads();
   }
