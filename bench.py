@@ -214,17 +214,19 @@ def run_device(args, rank: int, world: int) -> None:
     nat.require_device(dev)
     n_sets = max(1, min(args.sets, args.steps))
     sets = [make_set(1000 * rank + i, dev) for i in range(n_sets)]
-    ws = B.LayerWorkspace()
-    outs = {}
-    for name, m, n in LAYERS:
-        outs[name] = dict(packed=torch.empty(m, n // 2, dtype=torch.uint8, device=dev),
-                          scales=torch.empty(m, 1, dtype=torch.float16, device=dev),
-                          zero_points=torch.empty(m, 1, dtype=torch.int8, device=dev),
-                          stats=torch.empty(2, dtype=torch.float64, device=dev))
+    lanes = Lanes(args.streams, dev)
+    for lane in lanes.lanes:
+        for name, m, n in LAYERS:
+            lane.outs[name] = dict(packed=torch.empty(m, n // 2, dtype=torch.uint8, device=dev),
+                                   scales=torch.empty(m, 1, dtype=torch.float16, device=dev),
+                                   zero_points=torch.empty(m, 1, dtype=torch.int8, device=dev),
+                                   stats=torch.empty(3, dtype=torch.float64, device=dev))
 
     def step(i):
         for name, W, H in sets[i % n_sets]:
-            B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, out=outs[name], ws=ws)
+            with lanes.next() as lane:
+                B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, out=lane.outs[name],
+                                      ws=lane.ws, check=False)
 
     for i in range(args.warmup):
         step(i)
@@ -239,11 +241,14 @@ def run_device(args, rank: int, world: int) -> None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         e0.record()
+        lanes.fork()
         for i in range(args.steps):
             step(i)
+        lanes.join()
         e1.record()
         torch.cuda.synchronize(dev)
         launches = lib.ic_launch_count() - l0
+    lanes.check()
     if world > 1:
         torch.distributed.barrier()
     ms = e0.elapsed_time(e1)
@@ -255,7 +260,7 @@ def run_device(args, rank: int, world: int) -> None:
     del sets
     torch.cuda.empty_cache()
 
-    e2e = run_e2e(args, dev, ws, world)
+    e2e = run_e2e(args, dev, lanes, world)
     if rank != 0:
         return
     achieved, gemm_ms = dominant_gemm_tflops(dev)
@@ -272,7 +277,8 @@ def run_device(args, rank: int, world: int) -> None:
         "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic",
-        "config": dict(CONFIG, parallelism=f"layer sets sharded over {world} GPU(s), no collective"),
+        "config": dict(CONFIG, parallelism=f"layer sets sharded over {world} GPU(s), no collective",
+                       streams=args.streams),
         "e2e": e2e,
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
@@ -293,7 +299,57 @@ def run_device(args, rank: int, world: int) -> None:
 TRAFFIC_BYTES = None
 
 
-def run_e2e(args, dev: torch.device, ws, world: int) -> dict:
+class Lane:
+    def __init__(self, stream, dev):
+        import int_crush_converter_b200 as B
+        self.stream = stream
+        self.ws = B.LayerWorkspace()
+        self.outs = {}
+        self.results = []
+
+    def __enter__(self):
+        self._ctx = torch.cuda.stream(self.stream)
+        self._ctx.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        self._ctx.__exit__(*exc)
+
+
+class Lanes:
+    """Layers issued round-robin on S CUDA streams, each with its own workspace and
+    outputs, so that one layer's latency-bound steps (the inverse's diagonal
+    blocks, the column loop) overlap another layer's tensor-core GEMMs."""
+
+    def __init__(self, n: int, dev: torch.device):
+        self.dev = dev
+        streams = [torch.cuda.current_stream(dev)] if n <= 1 else [torch.cuda.Stream(dev) for _ in range(n)]
+        self.lanes = [Lane(s, dev) for s in streams]
+        self.k = 0
+
+    def next(self) -> Lane:
+        lane = self.lanes[self.k % len(self.lanes)]
+        self.k += 1
+        return lane
+
+    def fork(self):
+        cur = torch.cuda.current_stream(self.dev)
+        for lane in self.lanes:
+            lane.stream.wait_stream(cur)
+
+    def join(self):
+        cur = torch.cuda.current_stream(self.dev)
+        for lane in self.lanes:
+            cur.wait_stream(lane.stream)
+
+    def check(self):
+        import int_crush_converter_b200 as B
+        for lane in self.lanes:
+            for o in lane.outs.values():
+                B.check_layer(o)
+
+
+def run_e2e(args, dev: torch.device, lanes, world: int) -> dict:
     """Same metric through the public API with HOST buffers: every step copies one
     set's fp16 weights and fp32 Hessians from pinned host memory, quantizes, and
     reads back the packed codes, scales and zero-points."""
@@ -308,29 +364,40 @@ def run_e2e(args, dev: torch.device, ws, world: int) -> dict:
                      torch.empty(m, 1, dtype=torch.float16).pin_memory(),
                      torch.empty(m, 1, dtype=torch.int8).pin_memory())
     h2d = sum(W.numel() * 2 + H.numel() * 4 for _, W, H in host)
-    d2h = sum(p.numel() + s.numel() * 2 + z.numel() for p, s, z in res.values())
+    d2h = sum(p.numel() + s.numel() * 2 + z.numel() + 3 * 8 for p, s, z in res.values())
     steps = max(1, min(args.steps, args.e2e_steps))
 
     def step():
         for name, Wh, Hh in host:
-            W = Wh.to(dev, non_blocking=True)
-            H = Hh.to(dev, non_blocking=True)
-            o = B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, ws=ws)
-            p, s, z = res[name]
-            p.copy_(o["packed"], non_blocking=True)
-            s.copy_(o["scales"], non_blocking=True)
-            z.copy_(o["zero_points"], non_blocking=True)
+            with lanes.next() as lane:
+                W = Wh.to(dev, non_blocking=True)
+                H = Hh.to(dev, non_blocking=True)
+                o = B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, ws=lane.ws,
+                                          out=lane.outs[name], check=False)
+                p, s, z = res[name]
+                p.copy_(o["packed"], non_blocking=True)
+                s.copy_(o["scales"], non_blocking=True)
+                z.copy_(o["zero_points"], non_blocking=True)
+                st[name].copy_(o["stats"], non_blocking=True)
 
+    st = {name: torch.empty(3, dtype=torch.float64).pin_memory() for name, _, _ in LAYERS}
+    lanes.fork()
     step()
+    lanes.join()
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    lanes.fork()
     for _ in range(steps):
         step()
+    lanes.join()
     e1.record()
     torch.cuda.synchronize(dev)
+    for name, v in st.items():
+        if int(v[2]) & 2:
+            raise RuntimeError(f"{name}: Hessian is not positive definite")
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -347,6 +414,7 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--streams", type=int, default=4, help="CUDA streams the layers are issued on")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="time only the dominant 3xTF32 GEMM at n^3 (small profiling case)")
     args = ap.parse_args()

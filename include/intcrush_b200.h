@@ -182,8 +182,11 @@ int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw
  * column loop, pack, verify statistics.  H fp32 [N_in, N_in] (already in the
  * rotated space when h_rotated != 0).  Outputs: packed uint8 [M, npad/2]
  * (bits 4) and/or codes int8 [M, npad]; scales_f16 [M]; zp int8 [M] (bits 4
- * or asym); stats[2] fp64 = {mse, max_err} of the pipeline's verify step.
- * Synchronises once (reads the not-PD flag). */
+ * or asym).  With stats (fp64 [3] = {mse, max_err, status}: the pipeline's
+ * verify statistics and the layer's status bits, 2 = Hessian not positive
+ * definite) the call does not synchronise and the caller checks stats[2]
+ * (the reference then takes its inv/pinv branch); with stats == NULL it
+ * synchronises once and returns IC_ERR_NOT_PD. */
 size_t ic_gptq_layer_workspace_size(int64_t M, int64_t N_in, int rot);
 int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, int64_t ldw, const float* H,
                   int64_t ldh, int h_rotated, int rot, int bits, int asym, int block_size,

@@ -20,6 +20,8 @@ IC_OK = 0
 IC_ERR_INVALID = -1
 IC_ERR_CUDA = -2
 IC_ERR_NOT_PD = -3
+DEV_TIMEOUT = 1
+DEV_NOT_PD = 2
 IC_ERR_TIMEOUT = -4
 IC_ERR_RANGE = -5
 IC_ERR_UNSUPPORTED = -6

@@ -333,7 +333,7 @@ __global__ void copy_pair_kernel(const float* __restrict__ ih, const float* __re
 }
 
 __global__ void stats_kernel(const double* __restrict__ sq, const float* __restrict__ mx, int64_t M, double count,
-                             double* out) {
+                             double* out, const unsigned* status) {
   __shared__ double rs[32];
   __shared__ float rm[32];
   double s = 0.0;
@@ -356,6 +356,7 @@ __global__ void stats_kernel(const double* __restrict__ sq, const float* __restr
     }
     out[0] = count > 0 ? rs[0] / count : 0.0;
     out[1] = (double)rm[0];
+    if (status) out[2] = (double)*status;
   }
 }
 
@@ -497,6 +498,7 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
 struct LayerWs {
   float *W0, *Wk, *Hh, *Hl, *scale, *zp, *sscale, *rmx;
   double* rsq;
+  unsigned* status;
   void* loop;
   size_t loop_bytes;
   void* inv;
@@ -520,6 +522,7 @@ size_t layer_ws(int64_t M, int64_t N_in, int rot, LayerWs* out, void* base, size
   w.sscale = cv.take<float>(M);
   w.rmx = cv.take<float>(M);
   w.rsq = cv.take<double>(M);
+  w.status = cv.take<unsigned>(1);
   w.loop_bytes = loop_ws(M, npad, 128, LAYER_SB);
   w.loop = cv.take<char>(w.loop_bytes);
   w.inv_bytes = spd_inverse_ws(npad);
@@ -532,7 +535,7 @@ size_t layer_ws(int64_t M, int64_t N_in, int rot, LayerWs* out, void* base, size
 
 int finalize_stats(const double* row_sqerr, const float* row_maxerr, int64_t M, double count, double* stats,
                    cudaStream_t st) {
-  stats_kernel<<<1, 1024, 0, st>>>(row_sqerr, row_maxerr, M, count, stats);
+  stats_kernel<<<1, 1024, 0, st>>>(row_sqerr, row_maxerr, M, count, stats, nullptr);
   IC_CHECK_LAUNCH();
   return IC_OK;
 }
@@ -632,7 +635,10 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   params_out_kernel<<<grid1(M), 256, 0, st>>>(w.scale, has_zp ? w.zp : nullptr, M, scales_f16,
                                                has_zp ? zp_out : nullptr, w.sscale);
   IC_CHECK_LAUNCH();
-  IC_TRY(spd_inverse(w.Hh, w.Hl, npad, ldw, damping, w.inv, w.inv_bytes, st));
+  // With stats the call stays asynchronous: the inverse's not-positive-definite bit lands in
+  // stats[2].  Without stats it synchronises once to return IC_ERR_NOT_PD.
+  IC_CUDA(cudaMemsetAsync(w.status, 0, sizeof(unsigned), st));
+  IC_TRY(spd_inverse(w.Hh, w.Hl, npad, ldw, damping, w.inv, w.inv_bytes, st, w.status));
   LoopArgs L{};
   L.W = w.Wk; L.ldw = ldw; L.W0 = w.W0; L.ldw0 = ldw; L.M = M; L.N = npad; L.h_hi = w.Hh; L.h_lo = w.Hl;
   L.ldh = ldw; L.B = block_size; L.SB = (LAYER_SB / block_size) * block_size;
@@ -641,6 +647,14 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   L.codes = codes; L.ldq = npad; L.packed = bits == 4 ? packed : nullptr;
   L.ldp = (npad + 1) / 2; L.row_sqerr = w.rsq; L.row_maxerr = w.rmx; L.passes = 3; L.ldlq = false;
   IC_TRY(run_loop(L, w.loop, w.loop_bytes, st));
-  if (stats) IC_TRY(finalize_stats(w.rsq, w.rmx, M, (double)M * (double)npad, stats, st));
+  if (stats) {
+    stats_kernel<<<1, 1024, 0, st>>>(w.rsq, w.rmx, M, (double)M * (double)npad, stats, w.status);
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
+  unsigned f = 0;
+  IC_CUDA(cudaMemcpyAsync(&f, w.status, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+  IC_CUDA(cudaStreamSynchronize(st));
+  if (f & DEV_NOT_PD) return fail(IC_ERR_NOT_PD, "Hessian is not positive definite");
   return IC_OK;
 }

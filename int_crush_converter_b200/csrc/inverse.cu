@@ -377,11 +377,13 @@ int transpose(const float* in_hi, const float* in_lo, int64_t rows, int64_t cols
 }
 
 int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping, void* ws, size_t ws_bytes,
-                cudaStream_t st) {
+                cudaStream_t st, unsigned* status) {
   if (n <= 0) return IC_OK;
   if (!h_hi || !h_lo) return fail(IC_ERR_INVALID, "spd_inverse: hi/lo pair required");
   if (ldh % 4) return fail(IC_ERR_INVALID, "spd_inverse: ld must be a multiple of 4");
-  unsigned* flags = device_flags();
+  // Without a status word the call is synchronous and reports through the device's flag word;
+  // with one, a non-positive pivot is or-ed into *status and nothing is read back.
+  unsigned* flags = status ? status : device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
   Ctx c{};
   c.H = Pair{h_hi, h_lo};
@@ -392,7 +394,7 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   const size_t need = ws_layout(n, ldh, &c, ws, ws_bytes);
   if (ws_bytes < need) return fail(IC_ERR_WORKSPACE, "spd_inverse: workspace too small (%zu < %zu)", ws_bytes, need);
   unsigned prev = 0;
-  IC_TRY(read_and_clear_flags(&prev, st));
+  if (!status) IC_TRY(read_and_clear_flags(&prev, st));
   if (damping >= 0.f) {
     damp_kernel<<<1, 1024, 0, st>>>(h_hi, h_lo, n, ldh, damping);
     IC_CHECK_LAUNCH();
@@ -408,6 +410,7 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
     mirror_kernel<<<grid, dim3(32, 8), 0, st>>>(h_hi, h_lo, n, ldh);
     IC_CHECK_LAUNCH();
   }
+  if (status) return IC_OK;
   unsigned f = 0;
   IC_TRY(read_and_clear_flags(&f, st));
   if (f & DEV_TIMEOUT) return fail(IC_ERR_TIMEOUT, "spd_inverse: a tensor-core wait timed out");

@@ -251,15 +251,20 @@ _default_ws = LayerWorkspace()
 def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, int_bits: int = 4,
                         asymmetric: bool = False, block_size: int = 128, damping: float = 0.01,
                         h_rotated: bool = False, want_codes: bool = False, want_packed: bool = True,
-                        out: dict | None = None, ws: LayerWorkspace | None = None) -> dict:
+                        out: dict | None = None, ws: LayerWorkspace | None = None, check: bool = True) -> dict:
     """Fused GPTQ layer on the GPU: pipeline.py:547-559 + 702-809 + 919-931 + 1010-1013.
 
     W fp16/bf16/fp32 [out, in] (unrotated), H fp32 [in, in] (unrotated unless
     ``h_rotated``).  Returns a dict of device tensors: ``packed`` uint8
     [out, in_pad/2] (INT4), ``codes`` int8 [out, in_pad] (if asked),
     ``scales`` fp16 [out, 1], ``zero_points`` int8 [out, 1] or None, and
-    ``stats`` fp64 [mse, max_err] of the pipeline's verify step.  Pass ``out``
-    (a dict of preallocated tensors with those keys) to avoid allocations.
+    ``stats`` fp64 [mse, max_err, status] of the pipeline's verify step.  Pass
+    ``out`` (a dict of preallocated tensors with those keys) to avoid
+    allocations.  The device work is asynchronous on the current stream; with
+    ``check`` (default) the call synchronises and raises
+    :class:`NotPositiveDefinite` when the damped Hessian had no Cholesky
+    factor; with ``check=False`` the caller calls :func:`check_layer` later
+    (so that layers on several streams overlap).
     """
     dev = device_of(W, H)
     Wd = W.to(dev)
@@ -286,7 +291,7 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
         zp = torch.empty(M, 1, dtype=torch.int8, device=dev)
     stats = o.get("stats")
     if stats is None:
-        stats = torch.empty(2, dtype=torch.float64, device=dev)
+        stats = torch.empty(3, dtype=torch.float64, device=dev)
     lib = nat.load()
     need = lib.ic_gptq_layer_workspace_size(M, N, rot_size)
     wbuf = (ws or _default_ws).get(need, dev)
@@ -294,4 +299,17 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
                                 rot_size, int_bits, int(asymmetric), block_size, float(damping), nat.ptr(codes),
                                 nat.ptr(packed), s16.data_ptr(), nat.ptr(zp), stats.data_ptr(), wbuf.data_ptr(),
                                 wbuf.numel(), nat.stream_ptr(dev)), "gptq_layer")
-    return dict(packed=packed, codes=codes, scales=s16, zero_points=zp, stats=stats)
+    res = dict(packed=packed, codes=codes, scales=s16, zero_points=zp, stats=stats)
+    if check:
+        check_layer(res)
+    return res
+
+
+def check_layer(res: dict) -> dict:
+    """Raise :class:`NotPositiveDefinite` if a :func:`quantize_gptq_layer` result
+    reports a Hessian without a Cholesky factor (reads ``stats[2]``; synchronises
+    with the stream that produced it)."""
+    status = int(res["stats"][2].item())
+    if status & nat.DEV_NOT_PD:
+        raise nat.NotPositiveDefinite("Hessian is not positive definite")
+    return res

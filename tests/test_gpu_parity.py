@@ -269,6 +269,58 @@ def test_gptq_aggregate_proxy_vs_oracle():
     assert abs(tot_gpu / tot_ref - 1) < 0.005, tot_gpu / tot_ref
 
 
+def test_gptq_layer_not_pd_reported():
+    """A Hessian without a Cholesky factor: the asynchronous call reports it in
+    stats[2], the checked call raises, and the C call without stats returns
+    IC_ERR_NOT_PD."""
+    M, N = 64, 256
+    W = cu(gi.weight_outlier_cols(5, M, N)).half()
+    H = -torch.eye(N, device="cuda")
+    out = B.quantize_gptq_layer(W, H, rot_size=256, check=False)
+    torch.cuda.synchronize()
+    assert int(out["stats"][2].item()) & nat.DEV_NOT_PD
+    with pytest.raises(nat.NotPositiveDefinite):
+        B.quantize_gptq_layer(W, H, rot_size=256)
+    lib = nat.load()
+    ws = torch.empty(lib.ic_gptq_layer_workspace_size(M, N, 256), dtype=torch.uint8, device="cuda")
+    packed = torch.empty(M, N // 2, dtype=torch.uint8, device="cuda")
+    s16 = torch.empty(M, dtype=torch.float16, device="cuda")
+    zp = torch.empty(M, dtype=torch.int8, device="cuda")
+    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, 0, 256, 4, 0, 128, 0.01, None,
+                           packed.data_ptr(), s16.data_ptr(), zp.data_ptr(), None, ws.data_ptr(), ws.numel(),
+                           nat.stream_ptr(W.device))
+    assert st == nat.IC_ERR_NOT_PD
+    # a good Hessian afterwards is unaffected
+    Hg = cu(gi.hessian_lognormal(6, N, 2 * N))
+    assert int(B.quantize_gptq_layer(W, Hg, rot_size=256)["stats"][2].item()) == 0
+
+
+def test_gptq_layers_on_streams_match_serial():
+    """Layers issued on separate CUDA streams (own workspaces) give the same
+    codes, scales and statistics as the same layers issued one after another."""
+    shapes = [(256, 1024), (512, 512), (128, 2048)]
+    ins = [(cu(gi.weight_outlier_cols(30 + i, m, n)).half(), cu(gi.hessian_lognormal(40 + i, n, 2 * n)))
+           for i, (m, n) in enumerate(shapes)]
+    serial = [B.quantize_gptq_layer(W, H, rot_size=256, want_codes=True) for W, H in ins]
+    streams = [torch.cuda.Stream() for _ in ins]
+    wss = [B.LayerWorkspace() for _ in ins]
+    cur = torch.cuda.current_stream()
+    par = []
+    for (W, H), s, ws in zip(ins, streams, wss):
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            par.append(B.quantize_gptq_layer(W, H, rot_size=256, want_codes=True, ws=ws, check=False))
+    for s in streams:
+        cur.wait_stream(s)
+    torch.cuda.synchronize()
+    for a, b in zip(serial, par):
+        B.check_layer(b)
+        assert torch.equal(a["codes"], b["codes"])
+        assert torch.equal(a["packed"], b["packed"])
+        assert torch.equal(a["scales"], b["scales"])
+        assert torch.equal(a["stats"], b["stats"])
+
+
 # ---------------------------------------------------------------- LDLQ / greedy / PiSO
 @pytest.mark.parametrize("name", list(C.LDLQ_CASES))
 def test_ldlq(golden, name):
