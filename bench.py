@@ -214,22 +214,15 @@ def run_device(args, rank: int, world: int) -> None:
     nat.require_device(dev)
     n_sets = max(1, min(args.sets, args.steps))
     sets = [make_set(1000 * rank + i, dev) for i in range(n_sets)]
-    lanes = Lanes(args.streams, dev)
-    for lane in lanes.lanes:
-        for name, m, n in LAYERS:
-            lane.outs[name] = dict(packed=torch.empty(m, n // 2, dtype=torch.uint8, device=dev),
-                                   scales=torch.empty(m, 1, dtype=torch.float16, device=dev),
-                                   zero_points=torch.empty(m, 1, dtype=torch.int8, device=dev),
-                                   stats=torch.empty(3, dtype=torch.float64, device=dev))
+    pool = B.LayerStreams(args.streams, dev)
 
     def step(i):
         for name, W, H in sets[i % n_sets]:
-            with lanes.next() as lane:
-                B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, out=lane.outs[name],
-                                      ws=lane.ws, check=False)
+            pool.submit(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP)
 
-    for i in range(args.warmup):
-        step(i)
+    with pool:
+        for i in range(args.warmup):
+            step(i)
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
@@ -241,14 +234,14 @@ def run_device(args, rank: int, world: int) -> None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         e0.record()
-        lanes.fork()
+        pool.fork()
         for i in range(args.steps):
             step(i)
-        lanes.join()
+        pool.join()
         e1.record()
         torch.cuda.synchronize(dev)
         launches = lib.ic_launch_count() - l0
-    lanes.check()
+    pool.check()
     if world > 1:
         torch.distributed.barrier()
     ms = e0.elapsed_time(e1)
@@ -260,7 +253,7 @@ def run_device(args, rank: int, world: int) -> None:
     del sets
     torch.cuda.empty_cache()
 
-    e2e = run_e2e(args, dev, lanes, world)
+    e2e = run_e2e(args, dev, pool, world)
     if rank != 0:
         return
     achieved, gemm_ms = dominant_gemm_tflops(dev)
@@ -299,61 +292,10 @@ def run_device(args, rank: int, world: int) -> None:
 TRAFFIC_BYTES = None
 
 
-class Lane:
-    def __init__(self, stream, dev):
-        import int_crush_converter_b200 as B
-        self.stream = stream
-        self.ws = B.LayerWorkspace()
-        self.outs = {}
-        self.results = []
-
-    def __enter__(self):
-        self._ctx = torch.cuda.stream(self.stream)
-        self._ctx.__enter__()
-        return self
-
-    def __exit__(self, *exc):
-        self._ctx.__exit__(*exc)
-
-
-class Lanes:
-    """Layers issued round-robin on S CUDA streams, each with its own workspace and
-    outputs, so that one layer's latency-bound steps (the inverse's diagonal
-    blocks, the column loop) overlap another layer's tensor-core GEMMs."""
-
-    def __init__(self, n: int, dev: torch.device):
-        self.dev = dev
-        streams = [torch.cuda.current_stream(dev)] if n <= 1 else [torch.cuda.Stream(dev) for _ in range(n)]
-        self.lanes = [Lane(s, dev) for s in streams]
-        self.k = 0
-
-    def next(self) -> Lane:
-        lane = self.lanes[self.k % len(self.lanes)]
-        self.k += 1
-        return lane
-
-    def fork(self):
-        cur = torch.cuda.current_stream(self.dev)
-        for lane in self.lanes:
-            lane.stream.wait_stream(cur)
-
-    def join(self):
-        cur = torch.cuda.current_stream(self.dev)
-        for lane in self.lanes:
-            cur.wait_stream(lane.stream)
-
-    def check(self):
-        import int_crush_converter_b200 as B
-        for lane in self.lanes:
-            for o in lane.outs.values():
-                B.check_layer(o)
-
-
-def run_e2e(args, dev: torch.device, lanes, world: int) -> dict:
+def run_e2e(args, dev: torch.device, pool, world: int) -> dict:
     """Same metric through the public API with HOST buffers: every step copies one
     set's fp16 weights and fp32 Hessians from pinned host memory, quantizes, and
     reads back the packed codes, scales and zero-points."""
-    import int_crush_converter_b200 as B
     host = []
     for name, W, H in make_set(99, dev):
         host.append((name, W.cpu().pin_memory(), H.cpu().pin_memory()))
@@ -367,43 +309,39 @@ def run_e2e(args, dev: torch.device, lanes, world: int) -> dict:
     d2h = sum(p.numel() + s.numel() * 2 + z.numel() + 3 * 8 for p, s, z in res.values())
     steps = max(1, min(args.steps, args.e2e_steps))
 
+    st = {name: torch.empty(3, dtype=torch.float64).pin_memory() for name, _, _ in LAYERS}
+
     def step():
         for name, Wh, Hh in host:
-            with lanes.next() as lane:
-                W = Wh.to(dev, non_blocking=True)
-                H = Hh.to(dev, non_blocking=True)
-                o = B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP, ws=lane.ws,
-                                          out=lane.outs[name], check=False)
-                p, s, z = res[name]
+            p, s, z = res[name]
+
+            def fetch(o, p=p, s=s, z=z, name=name):
                 p.copy_(o["packed"], non_blocking=True)
                 s.copy_(o["scales"], non_blocking=True)
                 z.copy_(o["zero_points"], non_blocking=True)
                 st[name].copy_(o["stats"], non_blocking=True)
+            pool.submit(Wh, Hh, rot_size=ROT, block_size=BLOCK, damping=DAMP, then=fetch)
 
-    st = {name: torch.empty(3, dtype=torch.float64).pin_memory() for name, _, _ in LAYERS}
-    lanes.fork()
-    step()
-    lanes.join()
+    with pool:
+        step()
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    lanes.fork()
+    pool.fork()
     for _ in range(steps):
         step()
-    lanes.join()
+    pool.join()
     e1.record()
     torch.cuda.synchronize(dev)
-    for name, v in st.items():
-        if int(v[2]) & 2:
-            raise RuntimeError(f"{name}: Hessian is not positive definite")
+    pool.check()
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     val = PARAMS_PER_SET * steps * world / (float(t.item()) * 1e-3) / 1e6
     return {"value": round(val, 3), "unit": "Mparams/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "steps": steps, "api": "int_crush_converter_b200.quantize_gptq_layer (C ABI ic_gptq_layer)"}
+            "steps": steps, "api": "int_crush_converter_b200.LayerStreams.submit -> quantize_gptq_layer (C ABI ic_gptq_layer)"}
 
 
 def main() -> None:

@@ -6,7 +6,7 @@ arguments, return types and errors) and run hand-written CUDA kernels from
 path: without an sm_100 GPU or without the built library, calls raise.
 """
 
-from .gptq import gptq_quantize_layer, gptq_quantize_layer_rtn, quantize_gptq_layer, check_layer, LayerWorkspace
+from .gptq import gptq_quantize_layer, gptq_quantize_layer_rtn, quantize_gptq_layer, check_layer, LayerWorkspace, LayerStreams
 from .greedy import greedy_local_search, greedy_local_search_pytorch
 from .hessian import dlr_to_dense, invert_dense, woodbury_inverse
 from .ldlq import ldlq_quantize_layer

@@ -18,6 +18,8 @@ std::atomic<unsigned long long> g_launches{0};
 }  // namespace
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void add_launches(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+unsigned long long launches() { return g_launches.load(); }
 
 int fail(int code, const char* fmt, ...) {
   char buf[1024];

@@ -31,6 +31,8 @@ int fail(int code, const char* fmt, ...);
   } while (0)
 
 void count_launch();
+void add_launches(unsigned long long n);  // kernels a replayed CUDA graph runs
+unsigned long long launches();
 
 #define IC_CHECK_LAUNCH()                                                      \
   do {                                                                         \

@@ -11,6 +11,8 @@
 // Every mbarrier wait is bounded (globaltimer); on timeout the kernel records
 // DEV_TIMEOUT in the device status word and finishes without waiting further.
 // No TMA multicast is used anywhere: every CTA loads its own tiles.
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -117,6 +119,89 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])            \
       : "r"(taddr))
 
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+constexpr int EPI_LD = 132;  // staged row stride in floats (float4 writes by row-per-lane are conflict-free)
+constexpr int EPI_RB = 8;    // rows whose C loads are issued together
+
+__device__ __forceinline__ float epi_value(const GemmArgs& a, float s, float c) {
+  const float v = a.alpha * s;
+  return fmaf(a.beta, c, v);
+}
+
+// D[row, n0 + lane*4 .. +3] for the warp's 32 rows, from the staged sums.
+template <int BN>
+__device__ __forceinline__ void epilogue_rows(const GemmArgs& a, const float* stage, int rbase, int n0, int lane) {
+  static_assert(BN == 128, "one float4 per lane covers a 128-wide row");
+  const int col = n0 + lane * 4;
+  if (col >= a.n) return;
+  const bool read_c = a.beta != 0.f && a.c_hi != nullptr;
+  const bool full = a.vec && col + 4 <= a.n;
+  for (int rr = 0; rr < 32; rr += EPI_RB) {
+    float4 ch[EPI_RB], cl[EPI_RB];
+#pragma unroll
+    for (int i = 0; i < EPI_RB; ++i) {
+      const int row = rbase + rr + i;
+      ch[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      cl[i] = ch[i];
+      if (read_c && full && row < a.m) {
+        ch[i] = *reinterpret_cast<const float4*>(a.c_hi + (long long)row * a.ldc + col);
+        if (a.c_lo) cl[i] = *reinterpret_cast<const float4*>(a.c_lo + (long long)row * a.ldc + col);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < EPI_RB; ++i) {
+      const int row = rbase + rr + i;
+      if (row >= a.m) break;
+      const float4 sv = *reinterpret_cast<const float4*>(stage + (rr + i) * EPI_LD + lane * 4);
+      const float sx[4] = {sv.x, sv.y, sv.z, sv.w};
+      float* dh = a.d_hi + (long long)row * a.ldd + col;
+      float* dl = a.d_lo ? a.d_lo + (long long)row * a.ldd + col : nullptr;
+      if (full) {
+        float v[4];
+        if (read_c) {
+          const float cx[4] = {ch[i].x + cl[i].x, ch[i].y + cl[i].y, ch[i].z + cl[i].z, ch[i].w + cl[i].w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = epi_value(a, sx[t], cx[t]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = a.alpha * sx[t];
+        }
+        if (dl) {
+          float4 h, l;
+          split_tf32(v[0], h.x, l.x);
+          split_tf32(v[1], h.y, l.y);
+          split_tf32(v[2], h.z, l.z);
+          split_tf32(v[3], h.w, l.w);
+          *reinterpret_cast<float4*>(dh) = h;
+          *reinterpret_cast<float4*>(dl) = l;
+        } else {
+          *reinterpret_cast<float4*>(dh) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      } else {
+        for (int t = 0; t < 4 && col + t < a.n; ++t) {
+          float x = a.alpha * sx[t];
+          if (read_c) {
+            float cv = a.c_hi[(long long)row * a.ldc + col + t];
+            if (a.c_lo) cv += a.c_lo[(long long)row * a.ldc + col + t];
+            x = fmaf(a.beta, cv, x);
+          }
+          if (dl) {
+            float h, l;
+            split_tf32(x, h, l);
+            dh[t] = h;
+            dl[t] = l;
+          } else {
+            dh[t] = x;
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int PASSES>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
@@ -132,6 +217,7 @@ struct Cfg {
   static constexpr int CHUNK = 2;
   static constexpr int NACC = CHUNKED ? 2 : 1;
   static constexpr int TMEM_COLS = NACC * BN;
+  static_assert(4 * 32 * EPI_LD * 4 <= STAGES * STAGE_BYTES, "epilogue staging fits in the stages");
 };
 
 template <int BN, int PASSES>
@@ -188,6 +274,18 @@ __global__ void __launch_bounds__(256, 1)
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 4 && args.beta != 0.f && args.c_hi) {
+    // warm L2 with this tile's C rows while the main loop runs
+    const int row = m0 + (warp - 4) * 32 + lane;
+    if (row < args.m) {
+      for (int q = 0; q < BN / 32; ++q) {
+        const int col = n0 + q * 32;
+        if (col >= args.n) break;
+        prefetch_l2(args.c_hi + (long long)row * args.ldc + col);
+        if (args.c_lo) prefetch_l2(args.c_lo + (long long)row * args.ldc + col);
+      }
+    }
+  }
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
     for (int kt = 0; kt < ktiles; ++kt) {
@@ -243,7 +341,6 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     // ---------------- epilogue ----------------
     const int wq = warp - 4;  // TMEM lane quarter this warp may access
-    const int row = m0 + wq * 32 + lane;
     float sum[BN];
 #pragma unroll
     for (int j = 0; j < BN; ++j) sum[j] = 0.f;
@@ -270,64 +367,19 @@ __global__ void __launch_bounds__(256, 1)
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce_bar(b)) : "memory");
       }
     }
-    if (row < args.m) {
-      const float* crow_hi = args.c_hi ? args.c_hi + (long long)row * args.ldc : nullptr;
-      const float* crow_lo = args.c_lo ? args.c_lo + (long long)row * args.ldc : nullptr;
-      float* drow_hi = args.d_hi + (long long)row * args.ldd;
-      float* drow_lo = args.d_lo ? args.d_lo + (long long)row * args.ldd : nullptr;
-      const bool read_c = args.beta != 0.f && crow_hi != nullptr;
+    // Stage the row-per-thread sums through shared memory (the pipeline stages
+    // are idle once the last accumulator has landed), then walk the warp's 32
+    // rows with the lanes along the row: C/D accesses become row-contiguous
+    // and the C loads of RB rows are in flight together.
+    float* stage = reinterpret_cast<float*>(smem) + wq * (32 * EPI_LD);
+    if (alive) {
 #pragma unroll
-      for (int j4 = 0; j4 < BN / 4; ++j4) {
-        const int col = n0 + j4 * 4;
-        if (col >= args.n) break;
-        float v[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) v[t] = args.alpha * sum[j4 * 4 + t];
-        if (args.vec && col + 4 <= args.n) {
-          if (read_c) {
-            float4 cv = *reinterpret_cast<const float4*>(crow_hi + col);
-            if (crow_lo) {
-              const float4 cl = *reinterpret_cast<const float4*>(crow_lo + col);
-              cv.x += cl.x; cv.y += cl.y; cv.z += cl.z; cv.w += cl.w;
-            }
-            v[0] = fmaf(args.beta, cv.x, v[0]);
-            v[1] = fmaf(args.beta, cv.y, v[1]);
-            v[2] = fmaf(args.beta, cv.z, v[2]);
-            v[3] = fmaf(args.beta, cv.w, v[3]);
-          }
-          if (drow_lo) {
-            float4 h, l;
-            split_tf32(v[0], h.x, l.x);
-            split_tf32(v[1], h.y, l.y);
-            split_tf32(v[2], h.z, l.z);
-            split_tf32(v[3], h.w, l.w);
-            *reinterpret_cast<float4*>(drow_hi + col) = h;
-            *reinterpret_cast<float4*>(drow_lo + col) = l;
-          } else {
-            *reinterpret_cast<float4*>(drow_hi + col) = make_float4(v[0], v[1], v[2], v[3]);
-          }
-        } else {
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (col + t >= args.n) break;
-            float x = v[t];
-            if (read_c) {
-              float cv = crow_hi[col + t];
-              if (crow_lo) cv += crow_lo[col + t];
-              x = fmaf(args.beta, cv, x);
-            }
-            if (drow_lo) {
-              float h, l;
-              split_tf32(x, h, l);
-              drow_hi[col + t] = h;
-              drow_lo[col + t] = l;
-            } else {
-              drow_hi[col + t] = x;
-            }
-          }
-        }
-      }
+      for (int j4 = 0; j4 < BN / 4; ++j4)
+        *reinterpret_cast<float4*>(stage + lane * EPI_LD + j4 * 4) =
+            make_float4(sum[j4 * 4], sum[j4 * 4 + 1], sum[j4 * 4 + 2], sum[j4 * 4 + 3]);
     }
+    __syncwarp();
+    if (alive) epilogue_rows<BN>(args, stage, m0 + wq * 32, n0, lane);
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
@@ -373,16 +425,25 @@ int make_map(CUtensorMap* tm, const float* base, int64_t rows, int64_t k, int64_
   return IC_OK;
 }
 
+// dynamic shared memory opt-in, once per device (function attributes are per device)
+template <int BN, int PASSES>
+int prepare() {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  IC_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load() & bit) return IC_OK;
+  IC_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<BN, PASSES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<BN, PASSES>::SMEM));
+  done.fetch_or(bit);
+  return IC_OK;
+}
+
 template <int BN, int PASSES>
 int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
            const GemmArgs& a, cudaStream_t st) {
   using C = Cfg<BN, PASSES>;
-  static bool attr = false;
-  if (!attr) {
-    IC_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<BN, PASSES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 C::SMEM));
-    attr = true;
-  }
+  IC_TRY((prepare<BN, PASSES>()));
   dim3 grid((unsigned)cdiv(a.n, BN), (unsigned)cdiv(a.m, BM));
   gemm_tn_kernel<BN, PASSES><<<grid, 256, C::SMEM, st>>>(ah, al, bh, bl, a);
   IC_CHECK_LAUNCH();
@@ -392,6 +453,12 @@ int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+int gemm_prepare() {
+  IC_TRY((prepare<128, 3>()));
+  IC_TRY((prepare<128, 1>()));
+  return device_flags() ? IC_OK : fail(IC_ERR_CUDA, "device status word unavailable");
+}
 
 int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
             int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,

@@ -14,6 +14,8 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
             int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
             const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
             int64_t ldd, int passes, cudaStream_t st, int tri = 0);
+// per-device set-up of the GEMM kernels (attributes, status word); call outside stream capture
+int gemm_prepare();
 int transpose(const float* in_hi, const float* in_lo, int64_t rows, int64_t cols, int64_t ldi,
               float alpha, float* out_hi, float* out_lo, int64_t ldo, cudaStream_t st);
 int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping, void* ws,

@@ -12,6 +12,11 @@
 // value).  Only the 128 x 128 diagonal blocks are factored in shared memory;
 // their explicit inverses serve the leaves of the triangular solves.  Only
 // the lower triangle of H is read.  A non-positive pivot sets DEV_NOT_PD.
+#include <atomic>
+#include <cstdlib>
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -282,6 +287,18 @@ struct Ctx {
   Pair slot(int64_t off) const { return Linv.at((off / BASE) * BASE, 0, BASE); }
 };
 
+// dynamic shared memory opt-in of the base kernel, once per device
+int chol_prepare() {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  IC_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load() & bit) return IC_OK;
+  IC_CUDA(cudaFuncSetAttribute(chol_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BASE_SMEM));
+  done.fetch_or(bit);
+  return IC_OK;
+}
+
 int64_t split_point(int64_t n) { return std::max<int64_t>((n / 2 / BASE) * BASE, BASE); }
 
 int gemm3(const Ctx& c, int64_t m, int64_t n, int64_t k, float alpha, Pair A, int64_t lda, Pair B, int64_t ldb,
@@ -310,11 +327,7 @@ int trsm_rec(const Ctx& c, Pair X, int64_t m, int64_t ldx, int64_t off, int64_t 
 int chol_rec(const Ctx& c, int64_t off, int64_t n) {
   if (n <= BASE) {
     Pair A = c.H.at(off, off, c.ld), S = c.slot(off);
-    static bool attr = false;
-    if (!attr) {
-      IC_CUDA(cudaFuncSetAttribute(chol_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BASE_SMEM));
-      attr = true;
-    }
+    IC_TRY(chol_prepare());
     chol_base_kernel<<<1, 512, BASE_SMEM, c.st>>>(A.hi, A.lo, (int)n, c.ld, S.hi, S.lo, c.flags);
     IC_CHECK_LAUNCH();
     return IC_OK;
@@ -376,6 +389,113 @@ int transpose(const float* in_hi, const float* in_lo, int64_t rows, int64_t cols
   return IC_OK;
 }
 
+namespace {
+
+// Everything the inverse enqueues, on c.st.
+int inverse_body(const Ctx& c, int64_t n, float damping) {
+  if (damping >= 0.f) {
+    damp_kernel<<<1, 1024, 0, c.st>>>(c.H.hi, c.H.lo, n, c.ld, damping);
+    IC_CHECK_LAUNCH();
+  }
+  IC_CUDA(cudaMemsetAsync(c.U.hi, 0, (size_t)n * c.ld * 4, c.st));
+  IC_CUDA(cudaMemsetAsync(c.U.lo, 0, (size_t)n * c.ld * 4, c.st));
+  IC_TRY(chol_rec(c, 0, n));
+  IC_TRY(invt_rec(c, 0, n));
+  // H^-1 = U U^T: lower tiles only, K from the tile row (U is upper triangular), then mirror
+  IC_TRY(gemm3(c, n, n, n, 1.f, c.U, c.ld, c.U, c.ld, 0.f, c.H, c.ld, false, 3));
+  dim3 grid((unsigned)cdiv(n, 32), (unsigned)cdiv(n, 32));
+  mirror_kernel<<<grid, dim3(32, 8), 0, c.st>>>(c.H.hi, c.H.lo, n, c.ld);
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
+
+// The recursion issues ~n/128 * 14 kernels (about 2000 at n = 16384), each
+// small one short; issued one by one they fill the launch queue and block the
+// host thread, which then cannot feed other streams.  The asynchronous inverse
+// is therefore captured once per (device, n, ld, buffers, damping, status word)
+// into a CUDA graph and replayed with a single launch.  The cache holds up to
+// MAX_GRAPHS executables; evicting one synchronises the device first.
+struct InvGraph {
+  int dev;
+  int64_t n, ld;
+  const void *hh, *hl, *ws, *status;
+  size_t ws_bytes;
+  float damping;
+  cudaGraphExec_t exec;
+  unsigned long long kernels, used;
+  bool same(const InvGraph& o) const {
+    return dev == o.dev && n == o.n && ld == o.ld && hh == o.hh && hl == o.hl && ws == o.ws &&
+           status == o.status && ws_bytes == o.ws_bytes && damping == o.damping;
+  }
+};
+constexpr size_t MAX_GRAPHS = 32;
+std::mutex g_graph_mu;
+std::vector<InvGraph> g_graphs;
+unsigned long long g_tick = 0;
+cudaStream_t g_capture[64] = {nullptr};
+
+bool graphs_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("IC_GRAPHS");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_bytes) {
+  InvGraph key{};
+  IC_CUDA(cudaGetDevice(&key.dev));
+  key.n = n; key.ld = c.ld; key.hh = c.H.hi; key.hl = c.H.lo; key.ws = ws; key.status = c.flags;
+  key.ws_bytes = ws_bytes; key.damping = damping;
+  std::lock_guard<std::mutex> lock(g_graph_mu);
+  for (auto& g : g_graphs) {
+    if (g.same(key)) {
+      g.used = ++g_tick;
+      IC_CUDA(cudaGraphLaunch(g.exec, c.st));
+      add_launches(g.kernels);
+      return IC_OK;
+    }
+  }
+  // set-up that must not happen inside a capture
+  IC_TRY(gemm_prepare());
+  IC_TRY(chol_prepare());
+  if (key.dev < 0 || key.dev >= 64) return fail(IC_ERR_UNSUPPORTED, "device index %d", key.dev);
+  if (!g_capture[key.dev]) IC_CUDA(cudaStreamCreateWithFlags(&g_capture[key.dev], cudaStreamNonBlocking));
+  Ctx cc = c;
+  cc.st = g_capture[key.dev];
+  const unsigned long long k0 = launches();
+  IC_CUDA(cudaStreamBeginCapture(cc.st, cudaStreamCaptureModeThreadLocal));
+  const int r = inverse_body(cc, n, damping);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(cc.st, &graph);
+  if (r != IC_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return r;
+  }
+  if (e != cudaSuccess || !graph)
+    return fail(IC_ERR_CUDA, "spd_inverse: stream capture failed: %s", cudaGetErrorString(e));
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) return fail(IC_ERR_CUDA, "spd_inverse: graph instantiation failed: %s", cudaGetErrorString(ei));
+  key.exec = exec;
+  key.kernels = launches() - k0;  // counted while capturing; they run now, in the first replay
+  key.used = ++g_tick;
+  if (g_graphs.size() >= MAX_GRAPHS) {
+    size_t lru = 0;
+    for (size_t i = 1; i < g_graphs.size(); ++i)
+      if (g_graphs[i].used < g_graphs[lru].used) lru = i;
+    IC_CUDA(cudaDeviceSynchronize());
+    cudaGraphExecDestroy(g_graphs[lru].exec);
+    g_graphs.erase(g_graphs.begin() + (std::ptrdiff_t)lru);
+  }
+  g_graphs.push_back(key);
+  IC_CUDA(cudaGraphLaunch(exec, c.st));
+  return IC_OK;
+}
+
+}  // namespace
+
 int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping, void* ws, size_t ws_bytes,
                 cudaStream_t st, unsigned* status) {
   if (n <= 0) return IC_OK;
@@ -393,24 +513,15 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   // the workspace holds U with the caller's leading dimension
   const size_t need = ws_layout(n, ldh, &c, ws, ws_bytes);
   if (ws_bytes < need) return fail(IC_ERR_WORKSPACE, "spd_inverse: workspace too small (%zu < %zu)", ws_bytes, need);
+  if (status) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    IC_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (graphs_enabled() && cs == cudaStreamCaptureStatusNone) return inverse_graph(c, n, damping, ws, ws_bytes);
+    return inverse_body(c, n, damping);
+  }
   unsigned prev = 0;
-  if (!status) IC_TRY(read_and_clear_flags(&prev, st));
-  if (damping >= 0.f) {
-    damp_kernel<<<1, 1024, 0, st>>>(h_hi, h_lo, n, ldh, damping);
-    IC_CHECK_LAUNCH();
-  }
-  IC_CUDA(cudaMemsetAsync(c.U.hi, 0, (size_t)n * ldh * 4, st));
-  IC_CUDA(cudaMemsetAsync(c.U.lo, 0, (size_t)n * ldh * 4, st));
-  IC_TRY(chol_rec(c, 0, n));
-  IC_TRY(invt_rec(c, 0, n));
-  // H^-1 = U U^T: lower tiles only, K from the tile row (U is upper triangular), then mirror
-  IC_TRY(gemm3(c, n, n, n, 1.f, c.U, ldh, c.U, ldh, 0.f, c.H, ldh, false, 3));
-  {
-    dim3 grid((unsigned)cdiv(n, 32), (unsigned)cdiv(n, 32));
-    mirror_kernel<<<grid, dim3(32, 8), 0, st>>>(h_hi, h_lo, n, ldh);
-    IC_CHECK_LAUNCH();
-  }
-  if (status) return IC_OK;
+  IC_TRY(read_and_clear_flags(&prev, st));
+  IC_TRY(inverse_body(c, n, damping));
   unsigned f = 0;
   IC_TRY(read_and_clear_flags(&f, st));
   if (f & DEV_TIMEOUT) return fail(IC_ERR_TIMEOUT, "spd_inverse: a tensor-core wait timed out");

@@ -313,3 +313,89 @@ def check_layer(res: dict) -> dict:
     if status & nat.DEV_NOT_PD:
         raise nat.NotPositiveDefinite("Hessian is not positive definite")
     return res
+
+
+class LayerStreams:
+    """Quantize independent layers concurrently on several CUDA streams.
+
+    The reference quantizes a model's linear layers one after another
+    (pipeline.py:702-809 inside the per-layer loop); layers are independent
+    given their Hessians, so on the GPU they may overlap: one layer's
+    latency-bound steps (the inverse's 128-wide diagonal blocks, the GPTQ
+    column loop) fill the SMs another layer's tensor-core GEMMs leave idle.
+    Each stream owns a :class:`LayerWorkspace`; each submitted layer goes to the
+    stream with the least estimated work queued (M*N^2 + N^3).  Used as a
+    context manager: entering orders the streams after the current stream,
+    leaving orders the current stream after them and raises
+    :class:`NotPositiveDefinite` for any layer whose Hessian had no Cholesky
+    factor (the one synchronisation).
+    """
+
+    def __init__(self, n_streams: int = 4, device=None):
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.streams = [torch.cuda.Stream(dev) for _ in range(max(1, n_streams))]
+        self.ws = [LayerWorkspace() for _ in self.streams]
+        self.load = [0.0] * len(self.streams)
+        self._stats: list[torch.Tensor] = []
+
+    def __enter__(self):
+        self.fork()
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        self.join()
+        if exc_type is None:
+            self.check()
+        return False
+
+    def fork(self) -> None:
+        """Order the streams after the work already queued on the current stream."""
+        cur = torch.cuda.current_stream(self.device)
+        for s in self.streams:
+            s.wait_stream(cur)
+        self.load = [0.0] * len(self.streams)
+
+    def join(self) -> None:
+        """Order the current stream after everything submitted (no host wait)."""
+        cur = torch.cuda.current_stream(self.device)
+        for s in self.streams:
+            cur.wait_stream(s)
+
+    def submit(self, W: torch.Tensor, H: torch.Tensor, then=None, **kw) -> dict:
+        """Issue :func:`quantize_gptq_layer` (same keyword arguments) on the least
+        loaded stream; host inputs are copied to the device on that stream
+        (asynchronously when pinned; keep them alive until :meth:`join`), and
+        ``then(result)`` runs on that stream right after (e.g. a copy of the
+        outputs to host memory).  Returns the (asynchronous) result."""
+        M, N = int(W.shape[0]), int(W.shape[1])
+        i = min(range(len(self.load)), key=self.load.__getitem__)
+        self.load[i] += float(M) * N * N + float(N) ** 3
+        s = self.streams[i]
+        with torch.cuda.stream(s):
+            if not W.is_cuda:
+                W = W.to(self.device, non_blocking=True)
+            else:
+                W.record_stream(s)
+            if not H.is_cuda:
+                H = H.to(self.device, non_blocking=True)
+            else:
+                H.record_stream(s)
+            res = quantize_gptq_layer(W, H, ws=self.ws[i], check=False, **kw)
+            if then is not None:
+                then(res)
+        self._stats.append(res["stats"])
+        return res
+
+    def check(self) -> None:
+        """Wait for the submitted layers; raise if any reported a non-PD Hessian."""
+        if not self._stats:
+            return
+        self.join()
+        st = torch.stack([s[2] for s in self._stats]).cpu()
+        self._stats = []
+        bad = [i for i, v in enumerate(st.tolist()) if int(v) & nat.DEV_NOT_PD]
+        if bad:
+            raise nat.NotPositiveDefinite(f"Hessian is not positive definite (layers {bad} of this batch)")

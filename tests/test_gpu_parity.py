@@ -296,29 +296,26 @@ def test_gptq_layer_not_pd_reported():
 
 
 def test_gptq_layers_on_streams_match_serial():
-    """Layers issued on separate CUDA streams (own workspaces) give the same
-    codes, scales and statistics as the same layers issued one after another."""
+    """Layers issued through LayerStreams (two streams, own workspaces, host and
+    device inputs) give the same codes, scales and statistics as the same
+    layers issued one after another; a non-PD Hessian among them raises at exit."""
     shapes = [(256, 1024), (512, 512), (128, 2048)]
     ins = [(cu(gi.weight_outlier_cols(30 + i, m, n)).half(), cu(gi.hessian_lognormal(40 + i, n, 2 * n)))
            for i, (m, n) in enumerate(shapes)]
     serial = [B.quantize_gptq_layer(W, H, rot_size=256, want_codes=True) for W, H in ins]
-    streams = [torch.cuda.Stream() for _ in ins]
-    wss = [B.LayerWorkspace() for _ in ins]
-    cur = torch.cuda.current_stream()
-    par = []
-    for (W, H), s, ws in zip(ins, streams, wss):
-        s.wait_stream(cur)
-        with torch.cuda.stream(s):
-            par.append(B.quantize_gptq_layer(W, H, rot_size=256, want_codes=True, ws=ws, check=False))
-    for s in streams:
-        cur.wait_stream(s)
-    torch.cuda.synchronize()
+    pool = B.LayerStreams(2)
+    with pool:
+        par = [pool.submit(W if i % 2 else W.cpu().pin_memory(), H, rot_size=256, want_codes=True)
+               for i, (W, H) in enumerate(ins)]
     for a, b in zip(serial, par):
-        B.check_layer(b)
         assert torch.equal(a["codes"], b["codes"])
         assert torch.equal(a["packed"], b["packed"])
         assert torch.equal(a["scales"], b["scales"])
         assert torch.equal(a["stats"], b["stats"])
+    with pytest.raises(nat.NotPositiveDefinite):
+        with pool:
+            pool.submit(*ins[0], rot_size=256)
+            pool.submit(ins[1][0], -torch.eye(512, device="cuda"), rot_size=256)
 
 
 # ---------------------------------------------------------------- LDLQ / greedy / PiSO
