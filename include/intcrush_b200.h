@@ -121,6 +121,17 @@ int ic_gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi,
                float beta, const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi,
                float* d_lo, int64_t ldd, int passes, void* stream);
 
+/* 3xTF32 ic_gemm_tn restricted by triangular structure, as the inverse uses
+ * it (no direct counterpart in the reference, whose LAPACK call hides these
+ * products): tri bit 0 computes only the output 128-tiles on or below the
+ * diagonal (others are left unspecified); bit 1 declares A upper triangular
+ * (row i zero left of column i), so each tile's K loop starts at its first
+ * row. */
+int ic_gemm_tn_tri(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi,
+                   const float* a_lo, int64_t lda, const float* b_hi, const float* b_lo,
+                   int64_t ldb, float beta, const float* c_hi, const float* c_lo, int64_t ldc,
+                   float* d_hi, float* d_lo, int64_t ldd, int tri, void* stream);
+
 /* ---------------------------------------------------- Hessian preparation */
 /* Damping + inverse of an SPD Hessian held as a TF32 hi/lo pair [n,n] (in
  * place, ldh a multiple of 4): H <- (H + damping*max(mean(diag H),1e-6)*I)^-1.

@@ -53,6 +53,8 @@ SIGNATURES = {
     "ic_unpack_int4": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "ic_gemm_tn": (_i32, [_i64, _i64, _i64, _f32, _vp, _vp, _i64, _vp, _vp, _i64, _f32, _vp, _vp,
                           _i64, _vp, _vp, _i64, _i32, _vp]),
+    "ic_gemm_tn_tri": (_i32, [_i64, _i64, _i64, _f32, _vp, _vp, _i64, _vp, _vp, _i64, _f32, _vp, _vp,
+                              _i64, _vp, _vp, _i64, _i32, _vp]),
     "ic_spd_inverse_workspace_size": (_sz, [_i64]),
     "ic_spd_inverse": (_i32, [_vp, _vp, _i64, _i64, _f32, _vp, _sz, _vp]),
     "ic_gptq_row_params": (_i32, [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),

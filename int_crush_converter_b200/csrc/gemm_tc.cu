@@ -1,10 +1,11 @@
 // D = beta*C + alpha * A * B^T on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA computes a 128 x BN tile.  Warp roles (256 threads):
+// One CTA computes a 128 x BN tile.  Warp roles (384 threads):
 //   warp 0   : TMA producer (one thread) -- K-major fp32 tiles, 128B swizzle
 //   warp 1   : MMA issuer (one thread)   -- tcgen05.mma.kind::tf32, M=128, N=BN, K=8
 //   warp 2   : TMEM allocator
-//   warps 4-7: epilogue -- tcgen05.ld 32x32b, beta*C + alpha*acc, store
+//   warps 4-11: epilogue -- two warps per TMEM lane quarter, 64 columns each:
+//              tcgen05.ld 32x32b, chunk sums, beta*C + alpha*acc, store
 // PASSES = 3 implements 3xTF32: operands arrive as hi/lo pairs (hi exactly
 // TF32) and the accumulator receives hi*hi + hi*lo + lo*hi, giving close to
 // fp32 accuracy (needed by the Hessian inverse and the GPTQ error feedback).
@@ -12,6 +13,7 @@
 // DEV_TIMEOUT in the device status word and finishes without waiting further.
 // No TMA multicast is used anywhere: every CTA loads its own tiles.
 #include <atomic>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -123,6 +125,36 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// Grouped tile order: consecutive CTAs take `group` row-tiles times all
+// column-tiles, column by column, so that a wave of CTAs reads a compact
+// patch of A and B rows (and re-reads it from L2) instead of one A row-tile
+// against every B tile.
+constexpr int GROUP_M = 16;      // 128-row tiles per group (single-CTA kernel)
+constexpr int PAIR_GROUP_M = 8;  // 256-row pair tiles per group
+__device__ __forceinline__ void tile_of(int id, int mt, int nt, int group, int& tm, int& tn) {
+  const int per = group * nt;
+  const int g = id / per;
+  const int first = g * group;
+  const int gm = min(group, mt - first);
+  const int local = id - g * per;
+  tm = first + local % gm;
+  tn = local / gm;
+}
+
+// Optional wait-time counters (build with -DIC_GEMM_PROFILE; off in the library)
+#ifdef IC_GEMM_PROFILE
+__device__ unsigned long long g_gemm_prof[8];
+#define IC_PROF_T0() const long long _prof_t0 = clock64()
+#define IC_PROF_ADD(i) atomicAdd(&g_gemm_prof[i], (unsigned long long)(clock64() - _prof_t0))
+#else
+#define IC_PROF_T0() \
+  do {               \
+  } while (0)
+#define IC_PROF_ADD(i) \
+  do {                 \
+  } while (0)
+#endif
+
 constexpr int EPI_LD = 132;  // staged row stride in floats (float4 writes by row-per-lane are conflict-free)
 constexpr int EPI_RB = 8;    // rows whose C loads are issued together
 
@@ -132,14 +164,14 @@ __device__ __forceinline__ float epi_value(const GemmArgs& a, float s, float c) 
 }
 
 // D[row, n0 + lane*4 .. +3] for the warp's 32 rows, from the staged sums.
-template <int BN>
+template <int BN, int ROWS>
 __device__ __forceinline__ void epilogue_rows(const GemmArgs& a, const float* stage, int rbase, int n0, int lane) {
   static_assert(BN == 128, "one float4 per lane covers a 128-wide row");
   const int col = n0 + lane * 4;
   if (col >= a.n) return;
   const bool read_c = a.beta != 0.f && a.c_hi != nullptr;
   const bool full = a.vec && col + 4 <= a.n;
-  for (int rr = 0; rr < 32; rr += EPI_RB) {
+  for (int rr = 0; rr < ROWS; rr += EPI_RB) {
     float4 ch[EPI_RB], cl[EPI_RB];
 #pragma unroll
     for (int i = 0; i < EPI_RB; ++i) {
@@ -202,6 +234,59 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& a, const float* st
   }
 }
 
+// One epilogue warp (8 per CTA: two per TMEM lane quarter q = warp % 4, each
+// owning 64 of the 128 accumulator columns).  It adds the chunk accumulators
+// of its rows/columns in fp32 registers (round to nearest), releasing each
+// chunk's accumulator with `release(b)`, then stages its sums in shared memory
+// and, after its partner warp has staged the other half, writes 16 of the
+// quarter's 32 rows of D.  Returns false if a wait timed out.
+template <int NACC, bool CHUNKED, typename Release>
+__device__ __forceinline__ void epilogue_warp(const GemmArgs& args, uint32_t tmem, unsigned char* smem, int warp,
+                                              int lane, int nchunks, int m0, int n0, uint32_t accf0,
+                                              Release release) {
+  const int q = warp & 3, h = (warp - 4) >> 2;
+  float sum[64];
+#pragma unroll
+  for (int j = 0; j < 64; ++j) sum[j] = 0.f;
+  bool alive = true;
+  for (int c = 0; c < nchunks; ++c) {
+    const int b = c % NACC;
+    if (!mbar_wait(accf0 + 8u * (uint32_t)b, (c / NACC) & 1, args.flags)) {
+      alive = false;
+      break;
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    uint32_t r0[32], r1[32];
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + h * 64);
+    IC_TMEM_LD32(taddr, r0);
+    IC_TMEM_LD32(taddr + 32, r1);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      sum[j] = __fadd_rn(sum[j], __uint_as_float(r0[j]));
+      sum[32 + j] = __fadd_rn(sum[32 + j], __uint_as_float(r1[j]));
+    }
+    if (CHUNKED) {
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncwarp();
+      if (lane == 0) release(b);
+    }
+  }
+  // Stage through shared memory (the pipeline stages are idle once the last
+  // accumulator has landed), then walk rows with the lanes along the row:
+  // C/D accesses become row-contiguous, the C loads of several rows in flight.
+  float* stage = reinterpret_cast<float*>(smem) + q * (32 * EPI_LD);
+  if (alive) {
+#pragma unroll
+    for (int j4 = 0; j4 < 16; ++j4)
+      *reinterpret_cast<float4*>(stage + lane * EPI_LD + h * 64 + j4 * 4) =
+          make_float4(sum[j4 * 4], sum[j4 * 4 + 1], sum[j4 * 4 + 2], sum[j4 * 4 + 3]);
+  }
+  // both warps of the quarter (64 threads) meet on named barrier 1 + q
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+  if (alive) epilogue_rows<128, 16>(args, stage + h * 16 * EPI_LD, m0 + q * 32 + h * 16, n0, lane);
+}
+
 template <int BN, int PASSES>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
@@ -215,13 +300,13 @@ struct Cfg {
   // over a long K its bias adds up; chunking bounds that to CHUNK*32 terms.
   static constexpr bool CHUNKED = PASSES == 3;
   static constexpr int CHUNK = 2;
-  static constexpr int NACC = CHUNKED ? 2 : 1;
+  static constexpr int NACC = CHUNKED ? 4 : 1;  // ring of accumulators: the epilogue may lag NACC-1 chunks
   static constexpr int TMEM_COLS = NACC * BN;
   static_assert(4 * 32 * EPI_LD * 4 <= STAGES * STAGE_BYTES, "epilogue staging fits in the stages");
 };
 
 template <int BN, int PASSES>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA_hi, const __grid_constant__ CUtensorMap tmA_lo,
                    const __grid_constant__ CUtensorMap tmB_hi, const __grid_constant__ CUtensorMap tmB_lo,
                    const GemmArgs args) {
@@ -233,12 +318,14 @@ __global__ void __launch_bounds__(256, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
   // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], then the TMEM slot
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * C::NACC);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM;
-  const int n0 = blockIdx.x * BN;
+  int tm, tn;
+  tile_of(blockIdx.x, (args.m + BM - 1) / BM, (args.n + BN - 1) / BN, GROUP_M, tm, tn);
+  const int m0 = tm * BM;
+  const int n0 = tn * BN;
   if ((args.tri & 1) && n0 > m0) return;  // strictly-upper tile of a symmetric/lower result
   const int kbase = (args.tri & 2) ? min(m0, args.k) : 0;
   const int ktiles = (args.k - kbase + BK - 1) / BK;
@@ -247,7 +334,7 @@ __global__ void __launch_bounds__(256, 1)
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
   auto accf_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + b); };
-  auto acce_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + 2 + b); };
+  auto acce_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + C::NACC + b); };
   auto a_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES); };
   auto b_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES); };
   auto a_lo = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES); };
@@ -258,9 +345,9 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::NACC; ++b) {
       mbar_init(accf_bar(b), 1);
-      mbar_init(acce_bar(b), 4);  // one arrival per epilogue warp
+      mbar_init(acce_bar(b), 8);  // one arrival per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -276,9 +363,9 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp >= 4 && args.beta != 0.f && args.c_hi) {
     // warm L2 with this tile's C rows while the main loop runs
-    const int row = m0 + (warp - 4) * 32 + lane;
+    const int row = m0 + (warp & 3) * 32 + lane;
     if (row < args.m) {
-      for (int q = 0; q < BN / 32; ++q) {
+      for (int q = 2 * ((warp - 4) >> 2); q < 2 * ((warp - 4) >> 2) + 2; ++q) {
         const int col = n0 + q * 32;
         if (col >= args.n) break;
         prefetch_l2(args.c_hi + (long long)row * args.ldc + col);
@@ -291,7 +378,13 @@ __global__ void __launch_bounds__(256, 1)
     for (int kt = 0; kt < ktiles; ++kt) {
       const int s = kt % STAGES;
       const uint32_t ph = (kt / STAGES) & 1;
-      if (kt >= STAGES && !mbar_wait(empty_bar(s), ph ^ 1, args.flags)) break;
+      bool ok_e = true;
+      {
+        IC_PROF_T0();
+        if (kt >= STAGES) ok_e = mbar_wait(empty_bar(s), ph ^ 1, args.flags);
+        IC_PROF_ADD(2);
+      }
+      if (!ok_e) break;
       mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
       const int kx = kbase + kt * BK;
       tma_load_2d(a_hi(s), &tmA_hi, kx, m0, full_bar(s));
@@ -306,21 +399,29 @@ __global__ void __launch_bounds__(256, 1)
     constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                ((uint32_t)(BM >> 4) << 24);
     bool ok = true;
+#ifdef IC_GEMM_PROFILE
+    const long long loop_t0 = clock64();
+#endif
     for (int kt = 0; kt < ktiles && ok; ++kt) {
       const int chunk = C::CHUNKED ? kt / CH : 0;
-      const int b = chunk & 1;
+      const int b = chunk % C::NACC;
       const bool first_in_chunk = C::CHUNKED ? (kt % CH == 0) : (kt == 0);
-      if (C::CHUNKED && first_in_chunk && chunk >= 2 &&
-          !mbar_wait(acce_bar(b), ((chunk >> 1) & 1) ^ 1, args.flags)) {
-        ok = false;
-        break;
+      {
+        IC_PROF_T0();
+        if (C::CHUNKED && first_in_chunk && chunk >= C::NACC &&
+            !mbar_wait(acce_bar(b), ((chunk / C::NACC) & 1) ^ 1, args.flags))
+          ok = false;
+        IC_PROF_ADD(1);
       }
+      if (!ok) break;
       const int s = kt % STAGES;
       const uint32_t ph = (kt / STAGES) & 1;
-      if (!mbar_wait(full_bar(s), ph, args.flags)) {
-        ok = false;
-        break;
+      {
+        IC_PROF_T0();
+        if (!mbar_wait(full_bar(s), ph, args.flags)) ok = false;
+        IC_PROF_ADD(0);
       }
+      if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;");
       const uint32_t acc = tmem + (uint32_t)(b * BN);
 #pragma unroll
@@ -338,54 +439,214 @@ __global__ void __launch_bounds__(256, 1)
       const bool last_in_chunk = C::CHUNKED ? (kt % CH == CH - 1 || kt == ktiles - 1) : (kt == ktiles - 1);
       if (last_in_chunk) mma_commit(accf_bar(b));
     }
+#ifdef IC_GEMM_PROFILE
+    atomicAdd(&g_gemm_prof[3], (unsigned long long)(clock64() - loop_t0));
+    atomicAdd(&g_gemm_prof[5], 1ull);
+#endif
   } else if (warp >= 4) {
     // ---------------- epilogue ----------------
-    const int wq = warp - 4;  // TMEM lane quarter this warp may access
-    float sum[BN];
-#pragma unroll
-    for (int j = 0; j < BN; ++j) sum[j] = 0.f;
-    bool alive = true;
-    for (int c = 0; c < nchunks && alive; ++c) {
-      const int b = c & 1;
-      if (!mbar_wait(accf_bar(b), (c >> 1) & 1, args.flags)) {
-        alive = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;");
-#pragma unroll
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(b * BN + cc * 32);
-        IC_TMEM_LD32(taddr, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sum[cc * 32 + j] = __fadd_rn(sum[cc * 32 + j], __uint_as_float(r[j]));
-      }
-      if (C::CHUNKED) {
-        asm volatile("tcgen05.fence::before_thread_sync;");
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce_bar(b)) : "memory");
-      }
-    }
-    // Stage the row-per-thread sums through shared memory (the pipeline stages
-    // are idle once the last accumulator has landed), then walk the warp's 32
-    // rows with the lanes along the row: C/D accesses become row-contiguous
-    // and the C loads of RB rows are in flight together.
-    float* stage = reinterpret_cast<float*>(smem) + wq * (32 * EPI_LD);
-    if (alive) {
-#pragma unroll
-      for (int j4 = 0; j4 < BN / 4; ++j4)
-        *reinterpret_cast<float4*>(stage + lane * EPI_LD + j4 * 4) =
-            make_float4(sum[j4 * 4], sum[j4 * 4 + 1], sum[j4 * 4 + 2], sum[j4 * 4 + 3]);
-    }
-    __syncwarp();
-    if (alive) epilogue_rows<BN>(args, stage, m0 + wq * 32, n0, lane);
+    epilogue_warp<C::NACC, C::CHUNKED>(args, tmem, smem, warp, lane, nchunks, m0, n0, accf_bar(0), [&](int b) {
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce_bar(b)) : "memory");
+    });
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 2) {
     asm volatile("tcgen05.fence::after_thread_sync;");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2): a cluster of two CTAs on two SMs
+// computes a 256 x 128 tile with one M=256 MMA stream issued by the leader
+// (cluster rank 0).  Each CTA stages its own 128 rows of A and its own 64 rows
+// of B (no multicast: every TMA load writes the issuing CTA's shared memory),
+// so per SM the operand bytes per MMA drop by a quarter and four stages fit.
+// Protocol:
+//   full[s]   leader only; the leader arrives with expect_tx of both CTAs'
+//             bytes, both CTAs' TMA loads complete_tx on it
+//   empty[s]  in each CTA; the MMA commit arrives on both (multicast mask 3)
+//   accf[b]   in each CTA; the MMA commit arrives on both
+//   acce[b]   leader only, 8 arrivals (4 epilogue warps x 2 CTAs)
+// Each CTA's epilogue reads its own TMEM (its 128 rows).  All waits are
+// bounded; both CTAs always reach the closing cluster barrier.
+struct PairCfg {
+  static constexpr int A_BYTES = BM * BK * 4;       // 128 rows of A per CTA
+  static constexpr int B_BYTES = 64 * BK * 4;       // 64 rows of B per CTA
+  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = 196608 / STAGE_BYTES;  // 4
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int CHUNK = 2;
+  static constexpr int NACC = 4;           // ring of four 128-column accumulators
+  static constexpr int TMEM_COLS = NACC * 128;
+  static_assert(4 * 32 * EPI_LD * 4 <= STAGES * STAGE_BYTES, "epilogue staging fits in the stages");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory, completing on the leader's barrier
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* tm, int x, int y,
+                                                 uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(leader_bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  const uint16_t mask = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(384, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi, const __grid_constant__ CUtensorMap tmA_lo,
+                     const __grid_constant__ CUtensorMap tmB_hi, const __grid_constant__ CUtensorMap tmB_lo,
+                     const GemmArgs args) {
+  using C = PairCfg;
+  constexpr int STAGES = C::STAGES;
+  constexpr int CH = C::CHUNK;
+  constexpr int BN = 128;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * C::NACC);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  int pm, pn;
+  tile_of(blockIdx.x >> 1, (args.m + 255) / 256, (args.n + BN - 1) / BN, PAIR_GROUP_M, pm, pn);
+  const int mp = pm * 256;  // first row of the pair's tile
+  const int m0 = mp + (int)rank * BM;
+  const int n0 = pn * BN;
+  // pair-uniform decisions (both CTAs run the same K loop)
+  if ((args.tri & 1) && n0 > mp + BM) return;  // both halves strictly upper
+  const int kbase = (args.tri & 2) ? min(mp, args.k) : 0;
+  const int ktiles = (args.k - kbase + BK - 1) / BK;
+  const int nchunks = (ktiles + CH - 1) / CH;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto accf_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + b); };
+  auto acce_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + C::NACC + b); };
+  auto a_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES); };
+  auto b_hi = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES); };
+  auto a_lo = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES); };
+  auto b_lo = [&](int s) { return smem_u32(smem + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < C::NACC; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 16);  // leader's copy is the one used: 8 epilogue warps x 2 CTAs
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  if (warp >= 4 && args.beta != 0.f && args.c_hi) {
+    const int row = m0 + (warp & 3) * 32 + lane;
+    if (row < args.m) {
+      for (int q = 2 * ((warp - 4) >> 2); q < 2 * ((warp - 4) >> 2) + 2; ++q) {
+        const int col = n0 + q * 32;
+        if (col >= args.n) break;
+        prefetch_l2(args.c_hi + (long long)row * args.ldc + col);
+        if (args.c_lo) prefetch_l2(args.c_lo + (long long)row * args.ldc + col);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int s = kt % STAGES;
+      const uint32_t ph = (kt / STAGES) & 1;
+      if (kt >= STAGES && !mbar_wait(empty_bar(s), ph ^ 1, args.flags)) break;
+      if (leader) mbar_expect_tx(full_bar(s), 2 * C::STAGE_BYTES);
+      const uint32_t fb = map_to_rank(full_bar(s), 0);
+      const int kx = kbase + kt * BK;
+      const int nb = n0 + (int)rank * 64;
+      tma_load_2d_pair(a_hi(s), &tmA_hi, kx, m0, fb);
+      tma_load_2d_pair(b_hi(s), &tmB_hi, kx, nb, fb);
+      tma_load_2d_pair(a_lo(s), &tmA_lo, kx, m0, fb);
+      tma_load_2d_pair(b_lo(s), &tmB_lo, kx, nb, fb);
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------- MMA issuer (leader only) ----------------
+    constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                               ((uint32_t)(256 >> 4) << 24);
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int chunk = kt / CH;
+      const int b = chunk % C::NACC;
+      const bool first_in_chunk = kt % CH == 0;
+      if (first_in_chunk && chunk >= C::NACC && !mbar_wait(acce_bar(b), ((chunk / C::NACC) & 1) ^ 1, args.flags))
+        break;
+      const int s = kt % STAGES;
+      const uint32_t ph = (kt / STAGES) & 1;
+      if (!mbar_wait(full_bar(s), ph, args.flags)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const uint32_t acc = tmem + (uint32_t)(b * BN);
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t off = kk * 32;
+        const uint64_t ah = sdesc(a_hi(s) + off), bh = sdesc(b_hi(s) + off);
+        const uint64_t al = sdesc(a_lo(s) + off), bl = sdesc(b_lo(s) + off);
+        mma_tf32_pair(acc, ah, bh, idesc, (first_in_chunk && kk == 0) ? 0u : 1u);
+        mma_tf32_pair(acc, ah, bl, idesc, 1u);
+        mma_tf32_pair(acc, al, bh, idesc, 1u);
+      }
+      mma_commit_pair(empty_bar(s));
+      if (kt % CH == CH - 1 || kt == ktiles - 1) mma_commit_pair(accf_bar(b));
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue (both CTAs, own rows) ----------------
+    epilogue_warp<C::NACC, true>(args, tmem, smem, warp, lane, nchunks, m0, n0, accf_bar(0), [&](int b) {
+      remote_arrive(map_to_rank(acce_bar(b), 0));
+    });
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers or read its operands
+  if (warp == 2) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
 }
 
@@ -444,10 +705,56 @@ int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, 
            const GemmArgs& a, cudaStream_t st) {
   using C = Cfg<BN, PASSES>;
   IC_TRY((prepare<BN, PASSES>()));
-  dim3 grid((unsigned)cdiv(a.n, BN), (unsigned)cdiv(a.m, BM));
-  gemm_tn_kernel<BN, PASSES><<<grid, 256, C::SMEM, st>>>(ah, al, bh, bl, a);
+  const int64_t tiles = cdiv(a.n, BN) * cdiv(a.m, BM);
+  if (tiles > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "gemm: too many tiles");
+  gemm_tn_kernel<BN, PASSES><<<(unsigned)tiles, 384, C::SMEM, st>>>(ah, al, bh, bl, a);
   IC_CHECK_LAUNCH();
   return IC_OK;
+}
+
+int prepare_pair() {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  IC_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load() & bit) return IC_OK;
+  IC_CUDA(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM));
+  done.fetch_or(bit);
+  return IC_OK;
+}
+
+int launch_pair(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+                const GemmArgs& a, cudaStream_t st) {
+  IC_TRY(prepare_pair());
+  cudaLaunchConfig_t cfg{};
+  const int64_t ctas = 2 * cdiv(a.n, 128) * cdiv(a.m, 256);
+  if (ctas > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "gemm: too many tiles");
+  cfg.gridDim = dim3((unsigned)ctas, 1, 1);
+  cfg.blockDim = dim3(384, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;  // the CTA pair lies along the cluster's x
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  IC_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ah, al, bh, bl, a));
+  IC_CHECK_LAUNCH();
+  return IC_OK;
+}
+
+// CTA pairs for 3xTF32 products with more than one 128-row tile, opt-in with
+// IC_GEMM_PAIR=1: measured on B200 they match the single-CTA kernel on large
+// products (the main loop is tensor-bound either way) and lose on the many
+// one-tile products of the inverse's recursion.
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("IC_GEMM_PAIR");
+    return e && e[0] == '1';
+  }();
+  return on;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -457,6 +764,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int gemm_prepare() {
   IC_TRY((prepare<128, 3>()));
   IC_TRY((prepare<128, 1>()));
+  IC_TRY(prepare_pair());
   return device_flags() ? IC_OK : fail(IC_ERR_CUDA, "device status word unavailable");
 }
 
@@ -480,6 +788,13 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
              d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
+  if (passes == 3 && m > BM && pair_enabled()) {
+    IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
+    IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 64));
+    IC_TRY(make_map(&al, a_lo, m, kk, lda, BM));
+    IC_TRY(make_map(&bl, b_lo, n, kk, ldb, 64));
+    return launch_pair(ah, al, bh, bl, a, st);
+  }
   if (passes == 3) {
     IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
     IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 128));
@@ -500,4 +815,13 @@ extern "C" int ic_gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const fl
                           float* d_hi, float* d_lo, int64_t ldd, int passes, void* stream) {
   return ic::gemm_tn(m, n, k, alpha, a_hi, a_lo, lda, b_hi, b_lo, ldb, beta, c_hi, c_lo, ldc, d_hi, d_lo,
                      ldd, passes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ic_gemm_tn_tri(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi,
+                              const float* a_lo, int64_t lda, const float* b_hi, const float* b_lo,
+                              int64_t ldb, float beta, const float* c_hi, const float* c_lo, int64_t ldc,
+                              float* d_hi, float* d_lo, int64_t ldd, int tri, void* stream) {
+  if (tri < 0 || tri > 3) return ic::fail(IC_ERR_INVALID, "gemm: tri must be in [0,3]");
+  return ic::gemm_tn(m, n, k, alpha, a_hi, a_lo, lda, b_hi, b_lo, ldb, beta, c_hi, c_lo, ldc, d_hi, d_lo,
+                     ldd, 3, static_cast<cudaStream_t>(stream), tri);
 }

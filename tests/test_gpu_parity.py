@@ -41,7 +41,9 @@ def codes_close(a, b, max_frac=1e-4):
 
 # ---------------------------------------------------------------- GEMM
 @pytest.mark.parametrize("m,n,k,passes", [(128, 128, 32, 3), (300, 200, 100, 3), (128, 256, 1024, 1),
-                                          (513, 700, 260, 1), (1, 5, 7, 3), (256, 384, 2048, 3)])
+                                          (513, 700, 260, 1), (1, 5, 7, 3), (256, 384, 2048, 3),
+                                          (129, 64, 40, 3), (1000, 130, 128, 3), (768, 1024, 4096, 3),
+                                          (4096, 128, 128, 3)])
 def test_gemm_tn(m, n, k, passes):
     g = torch.Generator().manual_seed(m * 7 + n)
     A = torch.randn(m, k, generator=g).cuda()
@@ -59,6 +61,44 @@ def test_gemm_tn(m, n, k, passes):
     scale = 2.0 * Cm.double().abs() + 0.5 * (A.double().abs() @ Bm.double().abs().T)
     err = ((D.double() - ref).abs() / scale).max().item()
     assert err < (1e-5 if passes == 3 else 2e-3), err
+
+
+@pytest.mark.parametrize("tri", [1, 2, 3])
+@pytest.mark.parametrize("n", [384, 520])
+def test_gemm_triangular(n, tri):
+    """tri bit 0: only output 128-tiles on/below the diagonal are required;
+    bit 1: A is upper triangular and K starts at the tile row."""
+    g = torch.Generator().manual_seed(n + tri)
+    A = torch.randn(n, n, generator=g)
+    if tri & 2:
+        A = torch.triu(A)
+    A = A.cuda()
+    Bm = torch.randn(n, n, generator=g).cuda()
+    ah, al = split(A)
+    bh, bl = split(Bm)
+    D = torch.full((n, n), float("nan"), device="cuda")
+    ld = ah.shape[1]
+    nat.check(nat.load().ic_gemm_tn_tri(n, n, n, 1.0, ah.data_ptr(), al.data_ptr(), ld, bh.data_ptr(), bl.data_ptr(),
+                                        ld, 0.0, None, None, n, D.data_ptr(), None, n, tri, nat.stream_ptr(D.device)))
+    torch.cuda.synchronize()
+    ref = A.double() @ Bm.double().T
+    scale = A.double().abs() @ Bm.double().abs().T
+    r = torch.arange(n, device="cuda")
+    need = (r[None, :] // 128 <= r[:, None] // 128) if tri & 1 else torch.ones(n, n, dtype=torch.bool, device="cuda")
+    err = ((D.double() - ref).abs() / scale)[need]
+    assert not torch.isnan(err).any()
+    assert err.max().item() < 1e-5
+
+
+def test_gemm_cta_pair_kernel_subprocess():
+    """The cta_group::2 kernel (opt-in, IC_GEMM_PAIR=1) on the GEMM cases above."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, IC_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", __file__, "-k",
+                        "test_gemm_tn or test_gemm_triangular"], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 def test_gemm_pair_output():
