@@ -1,15 +1,16 @@
 // GPTQ / LDLQ column loop: rounding._gptq_block (converter/rounding.py:37-103)
 // and ldlq._ldlq_loop_cpu (converter/ldlq.py:369-417).
 //
-// Intra-block kernel: a CTA owns 32 weight rows (one per lane) and the whole
-// column block (<= 128 columns = 4 groups of 32, one warp per group, the
-// thread's 32 columns in registers).  The block's Hinv lives in shared
-// memory.  Groups are processed in order; inside the active group every
-// column is quantized and its normalised error applied eagerly to the group's
-// later columns, then the other warps apply the group's errors to their
-// columns, column by column in ascending order.  Every weight therefore sees
-// exactly the reference's sequence of fp32 operations
-// (w_k <- w_k - e_j * Hinv[j,k], a rounded multiply then a rounded subtract).
+// Intra-block kernel: one thread per weight row (a CTA owns 128 rows), the
+// block's <= 128 columns in four groups of 32.  The block's Hinv and the
+// CTA's block of W live in shared memory; the current group's 32 weights of
+// the row sit in registers.  Inside a group every column is quantized and its
+// normalised error applied at once to the group's later columns; then the
+// group's 32 errors are applied to the block's later columns, column by
+// column in ascending order.  Every weight therefore sees exactly the
+// reference's sequence of fp32 operations (w_k <- w_k - e_j * Hinv[j,k], a
+// rounded multiply then a rounded subtract).  Rows are independent, so no
+// thread ever waits for another after the loads.
 //
 // Inter-block update: W[:, after] -= E_blk * Hinv[blk, after] as tensor-core
 // GEMMs, two-level: "near" updates cover the rest of the current super-block
@@ -24,6 +25,7 @@ namespace {
 
 constexpr int GROUP = 32;
 constexpr int MAXB = 128;
+constexpr int ROWS = 128;  // weight rows (threads) per CTA of the block kernel
 
 struct BlockArgs {
   float* W;
@@ -54,211 +56,237 @@ struct BlockArgs {
 };
 
 template <bool LDLQ>
-__global__ void __launch_bounds__(128) block_kernel(const BlockArgs a) {
+__global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
   extern __shared__ float smem[];
-  float* hs = smem;                                      // [bc][MAXB] Hinv block (exact fp32)
-  float* es = smem + MAXB * MAXB;                        // [MAXB][32] errors (column j, lane)
-  float* dinv = es + MAXB * GROUP;                       // [MAXB] LDLQ: 1/max(Hinv[j,j],1e-8)
-  double* red = reinterpret_cast<double*>(dinv + MAXB);  // [4][32]
-  float* redm = reinterpret_cast<float*>(red + 4 * GROUP);
+  float* hs = smem;                // [MAXB][MAXB] Hinv block (exact fp32), row j = error column j
+  float* wsm = hs + MAXB * MAXB;   // [MAXB][ROWS] this CTA's weights of the block, column-major
+  float* dinv = wsm + MAXB * ROWS;  // [MAXB] LDLQ: 1/max(Hinv[j,j],1e-8)
 
-  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int t = threadIdx.x;
   const int bc = a.bc;
-  const int ng = (bc + GROUP - 1) / GROUP;
-  const int64_t r = (int64_t)blockIdx.x * GROUP + lane;
+  const int64_t r = (int64_t)blockIdx.x * ROWS + t;
   const bool rv = r < a.M;
   const int64_t rr = rv ? r : a.M - 1;  // clamp loads for the tail rows
 
   if (a.vec && bc == MAXB) {
-    // full 128 x 128 block: float4 loads, 32 per row, 8 in flight per thread
+    // full 128 x 128 block: float4 loads, 8 in flight per thread
     const float* hb = a.h_hi + a.i1 * a.ldh + a.i1;
     const float* lb = a.h_lo + a.i1 * a.ldh + a.i1;
-#pragma unroll 4
-    for (int it = 0; it < MAXB * MAXB / 4 / 128; it += 8) {
+#pragma unroll 1
+    for (int it = 0; it < MAXB * MAXB / 4 / ROWS; it += 8) {
       float4 hv[8], lv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int idx = (it + u) * 128 + threadIdx.x;
+        const int idx = (it + u) * ROWS + t;
         const int j = idx >> 5, k4 = (idx & 31) << 2;
         hv[u] = *reinterpret_cast<const float4*>(hb + j * a.ldh + k4);
         lv[u] = *reinterpret_cast<const float4*>(lb + j * a.ldh + k4);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int idx = (it + u) * 128 + threadIdx.x;
+        const int idx = (it + u) * ROWS + t;
         const int j = idx >> 5, k4 = (idx & 31) << 2;
-        float* d = hs + j * MAXB + k4;
-        d[0] = __fadd_rn(hv[u].x, lv[u].x);
-        d[1] = __fadd_rn(hv[u].y, lv[u].y);
-        d[2] = __fadd_rn(hv[u].z, lv[u].z);
-        d[3] = __fadd_rn(hv[u].w, lv[u].w);
+        *reinterpret_cast<float4*>(hs + j * MAXB + k4) =
+            make_float4(__fadd_rn(hv[u].x, lv[u].x), __fadd_rn(hv[u].y, lv[u].y), __fadd_rn(hv[u].z, lv[u].z),
+                        __fadd_rn(hv[u].w, lv[u].w));
+      }
+    }
+    // this row's 128 weights, 8 float4 loads in flight
+    const float4* wrow = reinterpret_cast<const float4*>(a.W + rr * a.ldw + a.i1);
+#pragma unroll 1
+    for (int c4 = 0; c4 < MAXB / 4; c4 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = wrow[c4 + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = 4 * (c4 + u);
+        wsm[c * ROWS + t] = v[u].x;
+        wsm[(c + 1) * ROWS + t] = v[u].y;
+        wsm[(c + 2) * ROWS + t] = v[u].z;
+        wsm[(c + 3) * ROWS + t] = v[u].w;
       }
     }
   } else {
     for (int j = 0; j < bc; ++j)
-      for (int k = threadIdx.x; k < bc; k += blockDim.x) {
+      for (int k = t; k < bc; k += ROWS) {
         const int64_t o = (a.i1 + j) * a.ldh + a.i1 + k;
         hs[j * MAXB + k] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
       }
+    const float* wrow = a.W + rr * a.ldw + a.i1;
+    for (int c = 0; c < bc; ++c) wsm[c * ROWS + t] = wrow[c];
   }
   __syncthreads();
   if (LDLQ)
-    for (int j = threadIdx.x; j < bc; j += blockDim.x) dinv[j] = __fdiv_rn(1.0f, fmaxf(hs[j * MAXB + j], 1e-8f));
+    for (int j = t; j < bc; j += ROWS) dinv[j] = __fdiv_rn(1.0f, fmaxf(hs[j * MAXB + j], 1e-8f));
+  if (LDLQ) __syncthreads();
 
-  const int cbase = g * GROUP;  // first block-local column of this thread
-  float w[GROUP], ev[GROUP];
-  float sc[LDLQ ? GROUP : 1];
-  const float* wrow = a.W + rr * a.ldw + a.i1 + cbase;
-  if (a.vec && cbase + GROUP <= bc) {
-#pragma unroll
-    for (int c4 = 0; c4 < GROUP / 4; ++c4) {
-      const float4 v = reinterpret_cast<const float4*>(wrow)[c4];
-      w[4 * c4] = v.x;
-      w[4 * c4 + 1] = v.y;
-      w[4 * c4 + 2] = v.z;
-      w[4 * c4 + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < GROUP; ++c) w[c] = (cbase + c < bc) ? wrow[c] : 0.f;
-  }
-#pragma unroll
-  for (int c = 0; c < GROUP; ++c) {
-    ev[c] = 0.f;
-    if (LDLQ) sc[c] = (cbase + c < bc) ? fmaxf(a.scale2d[rr * a.lds + a.i1 + cbase + c], 1e-8f) : 1.f;
-  }
   const float s = LDLQ ? 1.f : a.scale[rr];
   const float z = (!LDLQ && a.zp) ? a.zp[rr] : 0.f;
   const bool has_zp = !LDLQ && a.zp != nullptr;
-  __syncthreads();
+  const bool want_stats = !LDLQ && (a.row_sqerr || a.row_maxerr) && a.W0 != nullptr;
+  const float sst = (!LDLQ && a.stat_scale) ? a.stat_scale[rr] : s;
+  double sq_tot = 0.0;
+  float mx = 0.f;
+  const int ng = (bc + GROUP - 1) / GROUP;
 
+#pragma unroll 1
   for (int G = 0; G < ng; ++G) {
-    if (g == G) {
+    const int cb = G * GROUP;  // first block-local column of the group
+    float w[GROUP], ev[GROUP];
+    float sc[LDLQ ? GROUP : 1];
 #pragma unroll
-      for (int c = 0; c < GROUP; ++c) {
-        const int j = cbase + c;
-        if (j < bc) {
-          const float x = w[c];
-          float q, e;
-          if (!LDLQ) {
-            float raw = __fdiv_rn(x, s);
-            if (has_zp) raw = __fadd_rn(raw, z);
-            q = clampf(rhaz(raw), a.qmin, a.qmax);
-            const float deq = has_zp ? __fmul_rn(__fsub_rn(q, z), s) : __fmul_rn(q, s);
-            e = __fdiv_rn(__fsub_rn(x, deq), hs[j * MAXB + j]);
-            e = clampf(e, -100.f, 100.f);  // ERR_CLAMP_RANGE
-            if (e != e) e = 0.f;           // nan_to_num
-          } else {
-            // rounding._ldlq_round_column (rounding.py:115-155)
-            const float ss = sc[c];
-            q = clampf(rhaz(__fdiv_rn(x, ss)), a.qmin, a.qmax);
-            const float qs = (q > 0.f) ? 1.f : (q < 0.f ? -1.f : 0.f);
-            const float xs = (x > 0.f) ? 1.f : (x < 0.f ? -1.f : 0.f);
-            const float wsg = fabsf(x) > 1e-8f ? xs : qs;
-            const bool flip = wsg * qs < 0.f;
-            const bool can = flip && (q > a.qmin);
-            if (flip && q == a.qmin) q = a.qmax;
-            if (can) q = -q;
-            q = clampf(q, a.qmin, a.qmax);
-            e = __fmul_rn(__fsub_rn(x, __fmul_rn(q, ss)), dinv[j]);
-          }
-          w[c] = q;  // the weight itself is no longer needed
-          ev[c] = e;
-          es[j * GROUP + lane] = e;
+    for (int c = 0; c < GROUP; ++c) {
+      w[c] = (cb + c < bc) ? wsm[(cb + c) * ROWS + t] : 0.f;
+      if (LDLQ) sc[c] = (cb + c < bc) ? fmaxf(a.scale2d[rr * a.lds + a.i1 + cb + c], 1e-8f) : 1.f;
+    }
+    // the group's columns in order, each error applied at once to the group's later columns
+#pragma unroll 32
+    for (int c = 0; c < GROUP; ++c) {
+      const int j = cb + c;
+      ev[c] = 0.f;
+      if (j < bc) {
+        const float x = w[c];
+        float q, e;
+        if (!LDLQ) {
+          float raw = __fdiv_rn(x, s);
+          if (has_zp) raw = __fadd_rn(raw, z);
+          q = clampf(rhaz(raw), a.qmin, a.qmax);
+          const float deq = has_zp ? __fmul_rn(__fsub_rn(q, z), s) : __fmul_rn(q, s);
+          e = __fdiv_rn(__fsub_rn(x, deq), hs[j * MAXB + j]);
+          e = clampf(e, -100.f, 100.f);  // ERR_CLAMP_RANGE
+          if (e != e) e = 0.f;           // nan_to_num
+        } else {
+          // rounding._ldlq_round_column (rounding.py:115-155)
+          const float ss = sc[c];
+          q = clampf(rhaz(__fdiv_rn(x, ss)), a.qmin, a.qmax);
+          const float qs = (q > 0.f) ? 1.f : (q < 0.f ? -1.f : 0.f);
+          const float xs = (x > 0.f) ? 1.f : (x < 0.f ? -1.f : 0.f);
+          const float wsg = fabsf(x) > 1e-8f ? xs : qs;
+          const bool flip = wsg * qs < 0.f;
+          const bool can = flip && (q > a.qmin);
+          if (flip && q == a.qmin) q = a.qmax;
+          if (can) q = -q;
+          q = clampf(q, a.qmin, a.qmax);
+          e = __fmul_rn(__fsub_rn(x, __fmul_rn(q, ss)), dinv[j]);
+        }
+        w[c] = q;  // the weight itself is no longer needed
+        ev[c] = e;
+#pragma unroll 31
+        for (int c2 = c + 1; c2 < GROUP; ++c2)
+          if (cb + c2 < bc) w[c2] = __fsub_rn(w[c2], __fmul_rn(e, hs[j * MAXB + cb + c2]));
+      }
+    }
+
+    // ---- outputs of the group (w[] holds the codes) ----
+    const int nvalid = min(GROUP, bc - cb);
+    if (rv) {
+      const int64_t col = a.i1 + cb;
+      if (a.codes) {
+        int8_t* dst = a.codes + r * a.ldq + col;
+        if (nvalid == GROUP && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+          uint32_t pk[8];
 #pragma unroll
-          for (int c2 = c + 1; c2 < GROUP; ++c2)
-            if (cbase + c2 < bc) w[c2] = __fsub_rn(w[c2], __fmul_rn(e, hs[j * MAXB + cbase + c2]));
+          for (int i = 0; i < 8; ++i)
+            pk[i] = ((uint32_t)(uint8_t)(int8_t)w[4 * i]) | ((uint32_t)(uint8_t)(int8_t)w[4 * i + 1] << 8) |
+                    ((uint32_t)(uint8_t)(int8_t)w[4 * i + 2] << 16) |
+                    ((uint32_t)(uint8_t)(int8_t)w[4 * i + 3] << 24);
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < GROUP; ++c)
+            if (c < nvalid) dst[c] = (int8_t)w[c];
         }
       }
-    }
-    __syncthreads();
-    if (g > G) {
-      const int jend = min(bc, (G + 1) * GROUP);
-#pragma unroll 1
-      for (int j = G * GROUP; j < jend; ++j) {
-        const float e = es[j * GROUP + lane];
-        const float* hrow = hs + j * MAXB + cbase;
+      if (a.packed) {  // col is even (packing here needs an even block size)
+        uint8_t* dst = a.packed + r * a.ldp + col / 2;
+        if (nvalid == GROUP && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+          uint32_t pk[4];
 #pragma unroll
-        for (int c = 0; c < GROUP; ++c) w[c] = __fsub_rn(w[c], __fmul_rn(e, hrow[c]));
+          for (int i = 0; i < 4; ++i) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v |= ((uint32_t)((int)w[8 * i + k] & 15)) << (4 * k);
+            pk[i] = v;
+          }
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < GROUP; c += 2)
+            if (c < nvalid) {
+              const int lo = (int)w[c] & 15;
+              const int hi = (c + 1 < nvalid) ? ((int)w[c + 1] & 15) : 0;
+              dst[c / 2] = (uint8_t)(lo | (hi << 4));
+            }
+        }
       }
-    }
-  }
-
-  // ---- outputs for this thread's columns (w[] now holds the codes) ----
-  const int nvalid = max(0, min(GROUP, bc - cbase));
-  if (rv && nvalid > 0) {
-    const int64_t col = a.i1 + cbase;
-    if (a.codes) {
-      int8_t* dst = a.codes + r * a.ldq + col;
-      if (nvalid == GROUP && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-        uint32_t pk[8];
+      if (a.e_hi) {
+        float* dh = a.e_hi + r * a.lde + cb;
+        float* dl = a.e_lo ? a.e_lo + r * a.lde + cb : nullptr;
+        if (nvalid == GROUP && dl && ((reinterpret_cast<uintptr_t>(dh) | reinterpret_cast<uintptr_t>(dl)) & 15) == 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          pk[i] = ((uint32_t)(uint8_t)(int8_t)w[4 * i]) | ((uint32_t)(uint8_t)(int8_t)w[4 * i + 1] << 8) |
-                  ((uint32_t)(uint8_t)(int8_t)w[4 * i + 2] << 16) | ((uint32_t)(uint8_t)(int8_t)w[4 * i + 3] << 24);
-        reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      } else {
+          for (int c = 0; c < GROUP; c += 4) {
+            float4 h, l;
+            split_tf32(ev[c], h.x, l.x);
+            split_tf32(ev[c + 1], h.y, l.y);
+            split_tf32(ev[c + 2], h.z, l.z);
+            split_tf32(ev[c + 3], h.w, l.w);
+            *reinterpret_cast<float4*>(dh + c) = h;
+            *reinterpret_cast<float4*>(dl + c) = l;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < GROUP; ++c)
+            if (c < nvalid) {
+              const float h = to_tf32(ev[c]);
+              dh[c] = h;
+              if (dl) dl[c] = __fsub_rn(ev[c], h);
+            }
+        }
+      }
+      if (want_stats) {
+        double sq = 0.0;
+        const float* w0 = a.W0 + r * a.ldw0 + col;
 #pragma unroll
         for (int c = 0; c < GROUP; ++c)
-          if (c < nvalid) dst[c] = (int8_t)w[c];
+          if (c < nvalid) {
+            const float deq = has_zp ? __fmul_rn(__fsub_rn(w[c], z), sst) : __fmul_rn(w[c], sst);
+            const float d = __fsub_rn(w0[c], deq);
+            sq += (double)d * (double)d;
+            mx = nmax(mx, fabsf(d));
+          }
+        sq_tot += sq;
       }
     }
-    if (a.packed) {  // col is even (packing here needs an even block size)
-      uint8_t* dst = a.packed + r * a.ldp + col / 2;
+
+    // ---- this group's errors into the block's later columns, in column order ----
+    const int cend = (bc + 3) & ~3;  // columns past bc are scratch (never read back)
+#pragma unroll 1
+    for (int c2 = cb + GROUP; c2 < cend; c2 += 4) {
+      float v0 = wsm[c2 * ROWS + t], v1 = wsm[(c2 + 1) * ROWS + t];
+      float v2 = wsm[(c2 + 2) * ROWS + t], v3 = wsm[(c2 + 3) * ROWS + t];
 #pragma unroll
-      for (int c = 0; c < GROUP; c += 2)
-        if (c < nvalid) {
-          const int lo = (int)w[c] & 15;
-          const int hi = (c + 1 < nvalid) ? ((int)w[c + 1] & 15) : 0;
-          dst[c / 2] = (uint8_t)(lo | (hi << 4));
-        }
-    }
-    if (a.e_hi) {
-      float* dh = a.e_hi + r * a.lde + cbase;
-      float* dl = a.e_lo ? a.e_lo + r * a.lde + cbase : nullptr;
-#pragma unroll
-      for (int c = 0; c < GROUP; ++c)
-        if (c < nvalid) {
-          const float h = to_tf32(ev[c]);
-          dh[c] = h;
-          if (dl) dl[c] = __fsub_rn(ev[c], h);
-        }
+      for (int j = 0; j < GROUP; ++j) {
+        const float4 h = *reinterpret_cast<const float4*>(hs + (cb + j) * MAXB + c2);
+        v0 = __fsub_rn(v0, __fmul_rn(ev[j], h.x));
+        v1 = __fsub_rn(v1, __fmul_rn(ev[j], h.y));
+        v2 = __fsub_rn(v2, __fmul_rn(ev[j], h.z));
+        v3 = __fsub_rn(v3, __fmul_rn(ev[j], h.w));
+      }
+      wsm[c2 * ROWS + t] = v0;
+      wsm[(c2 + 1) * ROWS + t] = v1;
+      wsm[(c2 + 2) * ROWS + t] = v2;
+      wsm[(c2 + 3) * ROWS + t] = v3;
     }
   }
-  if (!LDLQ && (a.row_sqerr || a.row_maxerr)) {
-    double sq = 0.0;
-    float mx = 0.f;
-    if (rv && a.W0) {
-      const float ss = a.stat_scale ? a.stat_scale[r] : s;
-      const float* w0 = a.W0 + r * a.ldw0 + a.i1 + cbase;
-#pragma unroll
-      for (int c = 0; c < GROUP; ++c)
-        if (c < nvalid) {
-          const float deq = has_zp ? __fmul_rn(__fsub_rn(w[c], z), ss) : __fmul_rn(w[c], ss);
-          const float d = __fsub_rn(w0[c], deq);
-          sq += (double)d * (double)d;
-          mx = nmax(mx, fabsf(d));
-        }
-    }
-    red[g * GROUP + lane] = sq;
-    redm[g * GROUP + lane] = mx;
-    __syncthreads();
-    if (g == 0 && rv) {
-      double t = 0.0;
-      float m = 0.f;
-      for (int i = 0; i < 4; ++i) {
-        t += red[i * GROUP + lane];
-        m = nmax(m, redm[i * GROUP + lane]);
-      }
-      if (a.row_sqerr) a.row_sqerr[r] += t;
-      if (a.row_maxerr) a.row_maxerr[r] = nmax(a.row_maxerr[r], m);
-    }
+  if (want_stats && rv) {
+    if (a.row_sqerr) a.row_sqerr[r] += sq_tot;
+    if (a.row_maxerr) a.row_maxerr[r] = nmax(a.row_maxerr[r], mx);
   }
 }
 
-constexpr size_t BLOCK_SMEM =
-    (size_t)MAXB * MAXB * 4 + (size_t)MAXB * GROUP * 4 + MAXB * 4 + 4 * GROUP * 8 + 4 * GROUP * 4;
+constexpr size_t BLOCK_SMEM = (size_t)MAXB * MAXB * 4 + (size_t)MAXB * ROWS * 4 + MAXB * 4;
 
 // ---- per-row scale / zero-point preparation (converter/gptq.py:254-317) ----
 __global__ void __launch_bounds__(256) row_params_kernel(const float* __restrict__ W, int64_t N, int64_t ldw,
@@ -452,7 +480,7 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (L.row_sqerr) fill_kernel_d<<<grid1(L.M), 256, 0, st>>>(L.row_sqerr, L.M, 0.0);
   if (L.row_maxerr) fill_kernel_f<<<grid1(L.M), 256, 0, st>>>(L.row_maxerr, L.M, 0.f);
   IC_CHECK_LAUNCH();
-  const unsigned nblk = (unsigned)cdiv(L.M, GROUP);
+  const unsigned nblk = (unsigned)cdiv(L.M, ROWS);
   for (int64_t sb = 0; sb < L.N; sb += SB) {
     const int64_t sbe = std::min<int64_t>(sb + SB, L.N);
     for (int64_t i1 = sb; i1 < sbe; i1 += L.B) {
@@ -466,8 +494,8 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
       a.lde = lde; a.row_sqerr = L.row_sqerr; a.row_maxerr = L.row_maxerr;
       a.vec = ((L.ldw | L.ldh | i1) & 3) == 0 && (reinterpret_cast<uintptr_t>(L.W) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(L.h_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(L.h_lo) & 15) == 0;
-      if (L.ldlq) block_kernel<true><<<nblk, 128, BLOCK_SMEM, st>>>(a);
-      else block_kernel<false><<<nblk, 128, BLOCK_SMEM, st>>>(a);
+      if (L.ldlq) block_kernel<true><<<nblk, ROWS, BLOCK_SMEM, st>>>(a);
+      else block_kernel<false><<<nblk, ROWS, BLOCK_SMEM, st>>>(a);
       IC_CHECK_LAUNCH();
       if (i2 < sbe) {  // near update inside the super-block (i1 % 4 == 0 here)
         IC_TRY(gemm_tn(L.M, sbe - i2, i2 - i1, -1.f, e_hi + (i1 - sb), e_lo + (i1 - sb), lde,
