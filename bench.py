@@ -14,6 +14,8 @@ Modes:
   python bench.py [--gpus N --steps K --warmup W]      B200 path (one process per GPU)
   python bench.py --impl reference ...                 the reference's CPU algorithm (oracle
                                                        restatement) on the host cores
+Layers are issued on four CUDA streams (LayerStreams), so consecutive steps
+overlap; the default 24 steps measure that steady state.
 Multi-GPU: each rank quantizes its own sets (layers are independent, weak
 scaling); timing is the max over ranks of the device-event time.
 """
@@ -33,6 +35,8 @@ import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+
+from int_crush_converter_b200.sharding import max_over_ranks  # noqa: E402
 
 # (name, out_features, in_features) of one DiT linear set (config 3)
 LAYERS = [("qkv", 12288, 4096), ("proj", 4096, 4096), ("mlp_up", 16384, 4096), ("mlp_down", 4096, 16384)]
@@ -244,11 +248,7 @@ def run_device(args, rank: int, world: int) -> None:
     pool.check()
     if world > 1:
         torch.distributed.barrier()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(e0.elapsed_time(e1), dev)
     value = PARAMS_PER_SET * args.steps * world / (ms_max * 1e-3) / 1e6
     del sets
     torch.cuda.empty_cache()
@@ -336,10 +336,7 @@ def run_e2e(args, dev: torch.device, pool, world: int) -> dict:
     e1.record()
     torch.cuda.synchronize(dev)
     pool.check()
-    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    val = PARAMS_PER_SET * steps * world / (float(t.item()) * 1e-3) / 1e6
+    val = PARAMS_PER_SET * steps * world / (max_over_ranks(e0.elapsed_time(e1), dev) * 1e-3) / 1e6
     return {"value": round(val, 3), "unit": "Mparams/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "steps": steps, "api": "int_crush_converter_b200.LayerStreams.submit -> quantize_gptq_layer (C ABI ic_gptq_layer)"}
 
@@ -347,7 +344,7 @@ def run_e2e(args, dev: torch.device, pool, world: int) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=24)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")

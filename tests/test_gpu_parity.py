@@ -415,3 +415,17 @@ def test_piso(golden, name):
         assert np.mean(np_(o[1]) == golden[name + "/zp"]) >= 0.95
     else:
         assert np.mean(np_(o) == golden[name + "/scales"]) >= 0.95
+
+
+def test_sharded_layers_world1_match_serial():
+    """sharding.quantize_layers_sharded (the multi-GPU entry, here one rank) gives
+    the serial results for every layer."""
+    from int_crush_converter_b200 import sharding as S
+    layers = {f"l{i}": (cu(gi.weight_outlier_cols(60 + i, m, n)).half(), cu(gi.hessian_lognormal(70 + i, n, 2 * n)))
+              for i, (m, n) in enumerate([(256, 512), (128, 1024), (384, 256)])}
+    got = S.quantize_layers_sharded(layers, 0, 1, streams=2, rot_size=256)
+    assert set(got) == set(layers)
+    for k, (W, H) in layers.items():
+        ref = B.quantize_gptq_layer(W, H, rot_size=256)
+        assert torch.equal(ref["packed"], got[k]["packed"])
+        assert torch.equal(ref["scales"], got[k]["scales"])
