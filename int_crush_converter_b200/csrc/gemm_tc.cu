@@ -36,6 +36,7 @@ struct GemmArgs {
   long long ldd;
   unsigned* flags;
   int vec;  // C/D rows 16-byte aligned: vectorised epilogue
+  int kofs;  // K index of column 0 of A/B in the full product (K-slab launches)
   int tri;  // bit 0: only output tiles on/below the diagonal (n0 <= m0);
             // bit 1: A rows are zero left of their own index (upper triangular
             //        A), so the K loop starts at the tile's first row m0
@@ -242,14 +243,15 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& a, const float* st
 // quarter's 32 rows of D.  Returns false if a wait timed out.
 template <int NACC, bool CHUNKED, typename Release>
 __device__ __forceinline__ void epilogue_warp(const GemmArgs& args, uint32_t tmem, unsigned char* smem, int warp,
-                                              int lane, int nchunks, int m0, int n0, uint32_t accf0,
-                                              Release release) {
+                                              int lane, int nchunks, int chunk0, int m0, int n0,
+                                              uint32_t accf0, Release release) {
   const int q = warp & 3, h = (warp - 4) >> 2;
   float sum[64];
 #pragma unroll
   for (int j = 0; j < 64; ++j) sum[j] = 0.f;
   bool alive = true;
-  for (int c = 0; c < nchunks; ++c) {
+  for (int cl = 0; cl < nchunks; ++cl) {
+    const int c = chunk0 + cl;  // global chunk index (accumulator ring slot and phase)
     const int b = c % NACC;
     if (!mbar_wait(accf0 + 8u * (uint32_t)b, (c / NACC) & 1, args.flags)) {
       alive = false;
@@ -322,14 +324,8 @@ __global__ void __launch_bounds__(384, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  int tm, tn;
-  tile_of(blockIdx.x, (args.m + BM - 1) / BM, (args.n + BN - 1) / BN, GROUP_M, tm, tn);
-  const int m0 = tm * BM;
-  const int n0 = tn * BN;
-  if ((args.tri & 1) && n0 > m0) return;  // strictly-upper tile of a symmetric/lower result
-  const int kbase = (args.tri & 2) ? min(m0, args.k) : 0;
-  const int ktiles = (args.k - kbase + BK - 1) / BK;
-  const int nchunks = C::CHUNKED ? (ktiles + CH - 1) / CH : (ktiles > 0 ? 1 : 0);
+  const int mt = (args.m + BM - 1) / BM, nt = (args.n + BN - 1) / BN;
+  const int ntiles = mt * nt;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -361,98 +357,127 @@ __global__ void __launch_bounds__(384, 1)
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 4 && args.beta != 0.f && args.c_hi) {
-    // warm L2 with this tile's C rows while the main loop runs
-    const int row = m0 + (warp & 3) * 32 + lane;
-    if (row < args.m) {
-      for (int q = 2 * ((warp - 4) >> 2); q < 2 * ((warp - 4) >> 2) + 2; ++q) {
-        const int col = n0 + q * 32;
-        if (col >= args.n) break;
-        prefetch_l2(args.c_hi + (long long)row * args.ldc + col);
-        if (args.c_lo) prefetch_l2(args.c_lo + (long long)row * args.ldc + col);
-      }
-    }
-  }
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    for (int kt = 0; kt < ktiles; ++kt) {
-      const int s = kt % STAGES;
-      const uint32_t ph = (kt / STAGES) & 1;
-      bool ok_e = true;
-      {
-        IC_PROF_T0();
-        if (kt >= STAGES) ok_e = mbar_wait(empty_bar(s), ph ^ 1, args.flags);
-        IC_PROF_ADD(2);
-      }
-      if (!ok_e) break;
-      mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
-      const int kx = kbase + kt * BK;
-      tma_load_2d(a_hi(s), &tmA_hi, kx, m0, full_bar(s));
-      tma_load_2d(b_hi(s), &tmB_hi, kx, n0, full_bar(s));
-      if (PASSES == 3) {
-        tma_load_2d(a_lo(s), &tmA_lo, kx, m0, full_bar(s));
-        tma_load_2d(b_lo(s), &tmB_lo, kx, n0, full_bar(s));
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
-    constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                               ((uint32_t)(BM >> 4) << 24);
-    bool ok = true;
-#ifdef IC_GEMM_PROFILE
-    const long long loop_t0 = clock64();
-#endif
-    for (int kt = 0; kt < ktiles && ok; ++kt) {
-      const int chunk = C::CHUNKED ? kt / CH : 0;
-      const int b = chunk % C::NACC;
-      const bool first_in_chunk = C::CHUNKED ? (kt % CH == 0) : (kt == 0);
-      {
-        IC_PROF_T0();
-        if (C::CHUNKED && first_in_chunk && chunk >= C::NACC &&
-            !mbar_wait(acce_bar(b), ((chunk / C::NACC) & 1) ^ 1, args.flags))
-          ok = false;
-        IC_PROF_ADD(1);
-      }
-      if (!ok) break;
-      const int s = kt % STAGES;
-      const uint32_t ph = (kt / STAGES) & 1;
-      {
-        IC_PROF_T0();
-        if (!mbar_wait(full_bar(s), ph, args.flags)) ok = false;
-        IC_PROF_ADD(0);
-      }
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      const uint32_t acc = tmem + (uint32_t)(b * BN);
-#pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
-        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
-        const uint64_t ah = sdesc(a_hi(s) + off), bh = sdesc(b_hi(s) + off);
-        mma_tf32(acc, ah, bh, idesc, (first_in_chunk && kk == 0) ? 0u : 1u);
-        if (PASSES == 3) {
-          const uint64_t al = sdesc(a_lo(s) + off), bl = sdesc(b_lo(s) + off);
-          mma_tf32(acc, ah, bl, idesc, 1u);
-          mma_tf32(acc, al, bh, idesc, 1u);
+  // Persistent over tiles: CTA b takes tiles b, b + grid, ...  The CTAs of a
+  // wave start their tiles together and run at the same rate, so the A/B
+  // panels a wave shares are re-read from L2 rather than DRAM.  Pipeline
+  // stages and accumulators continue across tiles (global counters kt_g, ch_g).
+  int kt_g = 0, ch_g = 0;
+  bool ok = true;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    int tm, tn;
+    tile_of(tile, mt, nt, GROUP_M, tm, tn);
+    const int m0 = tm * BM;
+    const int n0 = tn * BN;
+    if ((args.tri & 1) && n0 > m0) continue;  // strictly-upper tile of a symmetric/lower result
+    const int kbase = (args.tri & 2) ? min(max(m0 - args.kofs, 0), args.k) : 0;
+    const int ktiles = (args.k - kbase + BK - 1) / BK;
+    const int nchunks = C::CHUNKED ? (ktiles + CH - 1) / CH : (ktiles > 0 ? 1 : 0);
+
+    if (warp >= 4 && args.beta != 0.f && args.c_hi) {
+      // warm L2 with this tile's C rows while the main loop runs
+      const int row = m0 + (warp & 3) * 32 + lane;
+      if (row < args.m) {
+        for (int q = 2 * ((warp - 4) >> 2); q < 2 * ((warp - 4) >> 2) + 2; ++q) {
+          const int col = n0 + q * 32;
+          if (col >= args.n) break;
+          prefetch_l2(args.c_hi + (long long)row * args.ldc + col);
+          if (args.c_lo) prefetch_l2(args.c_lo + (long long)row * args.ldc + col);
         }
       }
-      mma_commit(empty_bar(s));
-      const bool last_in_chunk = C::CHUNKED ? (kt % CH == CH - 1 || kt == ktiles - 1) : (kt == ktiles - 1);
-      if (last_in_chunk) mma_commit(accf_bar(b));
     }
+    if (warp == 0 && lane == 0 && ok) {
+      // ---------------- TMA producer ----------------
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int g = kt_g + kt;
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1;
+        bool ok_e = true;
+        {
+          IC_PROF_T0();
+          if (g >= STAGES) ok_e = mbar_wait(empty_bar(s), ph ^ 1, args.flags);
+          IC_PROF_ADD(2);
+        }
+        if (!ok_e) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
+        const int kx = kbase + kt * BK;
+        tma_load_2d(a_hi(s), &tmA_hi, kx, m0, full_bar(s));
+        tma_load_2d(b_hi(s), &tmB_hi, kx, n0, full_bar(s));
+        if (PASSES == 3) {
+          tma_load_2d(a_lo(s), &tmA_lo, kx, m0, full_bar(s));
+          tma_load_2d(b_lo(s), &tmB_lo, kx, n0, full_bar(s));
+        }
+      }
+    } else if (warp == 1 && lane == 0 && ok) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                 ((uint32_t)(BM >> 4) << 24);
 #ifdef IC_GEMM_PROFILE
-    atomicAdd(&g_gemm_prof[3], (unsigned long long)(clock64() - loop_t0));
-    atomicAdd(&g_gemm_prof[5], 1ull);
+      const long long loop_t0 = clock64();
 #endif
-  } else if (warp >= 4) {
-    // ---------------- epilogue ----------------
-    epilogue_warp<C::NACC, C::CHUNKED>(args, tmem, smem, warp, lane, nchunks, m0, n0, accf_bar(0), [&](int b) {
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce_bar(b)) : "memory");
-    });
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;");
-  __syncthreads();
-  if (warp == 2) {
+      for (int kt = 0; kt < ktiles && ok; ++kt) {
+        const int chunk = ch_g + (C::CHUNKED ? kt / CH : 0);
+        const int b = chunk % C::NACC;
+        const bool first_in_chunk = C::CHUNKED ? (kt % CH == 0) : (kt == 0);
+        {
+          IC_PROF_T0();
+          if (C::CHUNKED && first_in_chunk && chunk >= C::NACC &&
+              !mbar_wait(acce_bar(b), ((chunk / C::NACC) & 1) ^ 1, args.flags))
+            ok = false;
+          IC_PROF_ADD(1);
+        }
+        if (!ok) break;
+        const int g = kt_g + kt;
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1;
+        {
+          IC_PROF_T0();
+          if (!mbar_wait(full_bar(s), ph, args.flags)) ok = false;
+          IC_PROF_ADD(0);
+        }
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+          const uint64_t ah = sdesc(a_hi(s) + off), bh = sdesc(b_hi(s) + off);
+          mma_tf32(acc, ah, bh, idesc, (first_in_chunk && kk == 0) ? 0u : 1u);
+          if (PASSES == 3) {
+            const uint64_t al = sdesc(a_lo(s) + off), bl = sdesc(b_lo(s) + off);
+            mma_tf32(acc, ah, bl, idesc, 1u);
+            mma_tf32(acc, al, bh, idesc, 1u);
+          }
+        }
+        mma_commit(empty_bar(s));
+        const bool last_in_chunk =
+            C::CHUNKED ? (kt % CH == CH - 1 || kt == ktiles - 1) : (kt == ktiles - 1);
+        if (last_in_chunk) mma_commit(accf_bar(b));
+      }
+#ifdef IC_GEMM_PROFILE
+      atomicAdd(&g_gemm_prof[3], (unsigned long long)(clock64() - loop_t0));
+      atomicAdd(&g_gemm_prof[5], 1ull);
+#endif
+    } else if (warp >= 4) {
+      // ---------------- epilogue ----------------
+      epilogue_warp<C::NACC, C::CHUNKED>(args, tmem, smem, warp, lane, nchunks, ch_g, m0, n0, accf_bar(0),
+                                         [&](int b) {
+                                           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                                            acce_bar(b))
+                                                        : "memory");
+                                         });
+    }
+    kt_g += ktiles;
+    ch_g += nchunks;
+    // the epilogue staged through the pipeline's shared memory: the next
+    // tile's loads may only start once it is done
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
+  }
+  if (warp == 2) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
 }
@@ -548,7 +573,7 @@ __global__ void __launch_bounds__(384, 1)
   const int n0 = pn * BN;
   // pair-uniform decisions (both CTAs run the same K loop)
   if ((args.tri & 1) && n0 > mp + BM) return;  // both halves strictly upper
-  const int kbase = (args.tri & 2) ? min(mp, args.k) : 0;
+  const int kbase = (args.tri & 2) ? min(max(mp - args.kofs, 0), args.k) : 0;
   const int ktiles = (args.k - kbase + BK - 1) / BK;
   const int nchunks = (ktiles + CH - 1) / CH;
 
@@ -637,7 +662,7 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp >= 4) {
     // ---------------- epilogue (both CTAs, own rows) ----------------
-    epilogue_warp<C::NACC, true>(args, tmem, smem, warp, lane, nchunks, m0, n0, accf_bar(0), [&](int b) {
+    epilogue_warp<C::NACC, true>(args, tmem, smem, warp, lane, nchunks, 0, m0, n0, accf_bar(0), [&](int b) {
       remote_arrive(map_to_rank(acce_bar(b), 0));
     });
   }
@@ -700,6 +725,20 @@ int prepare() {
   return IC_OK;
 }
 
+// CTAs of a GEMM launch.  Default: one per tile.  IC_GEMM_CTAS=c makes the
+// kernel persistent with at most c CTAs.  Measured on B200 inside the
+// multi-stream layer pipeline, persistence lost 3-6%: resident CTAs hold SMs the
+// other streams' latency-bound kernels need, and the DRAM traffic of a 16384^3
+// product did not drop (167 GB either way).
+int persistent_ctas(int* out) {
+  static const int cap = [] {
+    const char* e = getenv("IC_GEMM_CTAS");
+    return (e && atoi(e) > 0) ? atoi(e) : INT32_MAX;
+  }();
+  *out = cap;
+  return IC_OK;
+}
+
 template <int BN, int PASSES>
 int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
            const GemmArgs& a, cudaStream_t st) {
@@ -707,7 +746,9 @@ int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, 
   IC_TRY((prepare<BN, PASSES>()));
   const int64_t tiles = cdiv(a.n, BN) * cdiv(a.m, BM);
   if (tiles > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "gemm: too many tiles");
-  gemm_tn_kernel<BN, PASSES><<<(unsigned)tiles, 384, C::SMEM, st>>>(ah, al, bh, bl, a);
+  int ctas = 0;
+  IC_TRY(persistent_ctas(&ctas));
+  gemm_tn_kernel<BN, PASSES><<<(unsigned)std::min<int64_t>(tiles, ctas), 384, C::SMEM, st>>>(ah, al, bh, bl, a);
   IC_CHECK_LAUNCH();
   return IC_OK;
 }
@@ -768,10 +809,11 @@ int gemm_prepare() {
   return device_flags() ? IC_OK : fail(IC_ERR_CUDA, "device status word unavailable");
 }
 
-int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
-            int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
-            const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
-            int64_t ldd, int passes, cudaStream_t st, int tri) {
+namespace {
+int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
+              int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
+              const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
+              int64_t ldd, int passes, cudaStream_t st, int tri, int kofs) {
   if (m <= 0 || n <= 0) return IC_OK;
   if (passes != 1 && passes != 3) return fail(IC_ERR_INVALID, "gemm: passes must be 1 or 3");
   if (passes == 3 && (!a_lo || !b_lo)) return fail(IC_ERR_INVALID, "gemm: 3xTF32 needs lo parts");
@@ -785,7 +827,7 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
   unsigned* flags = device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
   GemmArgs a{(int)m, (int)n, (int)(k > 0 ? k : 0), alpha, beta, c_hi, c_lo, (long long)ldc,
-             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tri};
+             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, kofs, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
   if (passes == 3 && m > BM && pair_enabled()) {
@@ -805,6 +847,40 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
   IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
   IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 128));
   return launch<128, 1>(ah, ah, bh, bh, a, st);
+}
+
+// K per launch for large products.  A 128-row operand panel of a long-K
+// product (128 x K x 8 bytes as a hi/lo pair: 16.8 MB at K = 16384) is too
+// large for the CTAs sharing it to find it in L2, so a 16384^3 product read
+// 167 GB from DRAM (38x its operands) on B200.  Split into K-slabs of this
+// width, each accumulating into D (as a hi/lo pair the running sum is exact
+// fp32, the same one rounding per slab as the kernel's chunk sums).
+// IC_GEMM_SLAB=0 turns the split off.
+int slab_k() {
+  static const int v = [] {
+    const char* e = getenv("IC_GEMM_SLAB");
+    return e ? atoi(e) : 4096;
+  }();
+  return v;
+}
+}  // namespace
+
+int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
+            int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
+            const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
+            int64_t ldd, int passes, cudaStream_t st, int tri) {
+  const int64_t sk = slab_k();
+  if (passes != 3 || sk <= 0 || sk % BK || k < 2 * sk || m * n < (int64_t(1) << 26))
+    return gemm_once(m, n, k, alpha, a_hi, a_lo, lda, b_hi, b_lo, ldb, beta, c_hi, c_lo, ldc, d_hi, d_lo, ldd,
+                     passes, st, tri, 0);
+  for (int64_t k0 = 0; k0 < k; k0 += sk) {
+    const int64_t kw = std::min(sk, k - k0);
+    const bool first = k0 == 0;
+    IC_TRY(gemm_once(m, n, kw, alpha, a_hi + k0, a_lo + k0, lda, b_hi + k0, b_lo + k0, ldb, first ? beta : 1.f,
+                     first ? c_hi : d_hi, first ? c_lo : d_lo, first ? ldc : ldd, d_hi, d_lo, ldd, passes, st,
+                     tri, (int)k0));
+  }
+  return IC_OK;
 }
 
 }  // namespace ic

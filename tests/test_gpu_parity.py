@@ -90,6 +90,39 @@ def test_gemm_triangular(n, tri):
     assert err.max().item() < 1e-5
 
 
+@pytest.mark.parametrize("tri", [0, 3])
+def test_gemm_k_slabs(tri):
+    """Products large enough to be split into K-slabs (m*n >= 2^26, k >= 8192),
+    plain and triangular, against an fp64 product on the GPU."""
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(5 + tri)
+    A = torch.randn(n, n, device="cuda", generator=g)
+    if tri & 2:
+        A = torch.triu(A)
+    Bm = torch.randn(n, n, device="cuda", generator=g)
+    ah, al = split(A)
+    bh, bl = split(Bm)
+    del A, Bm
+    D = torch.full((n, n), float("nan"), device="cuda")
+    Dl = torch.empty_like(D)
+    nat.check(nat.load().ic_gemm_tn_tri(n, n, n, 1.0, ah.data_ptr(), al.data_ptr(), n, bh.data_ptr(), bl.data_ptr(),
+                                        n, 0.0, None, None, n, D.data_ptr(), Dl.data_ptr(), n, tri,
+                                        nat.stream_ptr(D.device)))
+    torch.cuda.synchronize()
+    Ad = ah.double() + al.double()
+    Bd = bh.double() + bl.double()
+    rows = torch.arange(0, n, 1024, device="cuda")  # sampled rows keep the fp64 check cheap
+    ref = Ad[rows] @ Bd.T
+    scale = Ad[rows].abs() @ Bd.abs().T
+    got = D.double()[rows] + Dl.double()[rows]
+    err = (got - ref).abs() / scale
+    if tri & 1:
+        cols = torch.arange(n, device="cuda")
+        err = err[(cols[None, :] // 128) <= (rows[:, None] // 128)]
+    assert not torch.isnan(err).any()
+    assert err.max().item() < 1e-5
+
+
 def test_gemm_cta_pair_kernel_subprocess():
     """The cta_group::2 kernel (opt-in, IC_GEMM_PAIR=1) on the GEMM cases above."""
     import os
