@@ -12,10 +12,14 @@
 // rounded multiply then a rounded subtract).  Rows are independent, so no
 // thread ever waits for another after the loads.
 //
-// Inter-block update: W[:, after] -= E_blk * Hinv[blk, after] as tensor-core
-// GEMMs, two-level: "near" updates cover the rest of the current super-block
-// (L2-resident), one "far" update per super-block covers everything after it
-// with K = super-block width, so the fp32 W_work read-modify-write traffic is
+// Inter-block update as tensor-core GEMMs, two-level.  Inside a super-block
+// (1024 columns) the update is left-looking: before a block is quantized its
+// 128 columns take W[:, blk] -= E[:, sb:blk] * Hinv[sb:blk, blk] in one GEMM
+// whose K is everything processed so far in the super-block (the sum the
+// reference's lazy inter-block update, rounding.py:100-103, forms block by
+// block, with one rounding instead of one per block).  After the super-block, one "far"
+// update W[:, after] -= E_sb * Hinv[sb, after] with K = super-block width
+// covers every later column, so the fp32 W_work read-modify-write traffic is
 // divided by super-block / block.
 #include "common.cuh"
 #include "internal.h"
@@ -485,6 +489,11 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
     const int64_t sbe = std::min<int64_t>(sb + SB, L.N);
     for (int64_t i1 = sb; i1 < sbe; i1 += L.B) {
       const int64_t i2 = std::min<int64_t>(i1 + L.B, L.N);
+      if (i1 > sb) {  // left-looking near update: this block's columns take the super-block's earlier errors
+        IC_TRY(gemm_tn(L.M, i2 - i1, i1 - sb, -1.f, e_hi, e_lo, lde, L.h_hi + i1 * L.ldh + sb,
+                       L.h_lo + i1 * L.ldh + sb, L.ldh, 1.f, L.W + i1, nullptr, L.ldw, L.W + i1, nullptr, L.ldw,
+                       L.passes, st));
+      }
       BlockArgs a{};
       a.W = L.W; a.ldw = L.ldw; a.W0 = L.W0; a.ldw0 = L.ldw0; a.M = L.M; a.i1 = i1; a.bc = (int)(i2 - i1);
       a.h_hi = L.h_hi; a.h_lo = L.h_lo; a.ldh = L.ldh; a.scale = L.scale; a.zp = L.zp;
@@ -497,11 +506,6 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
       if (L.ldlq) block_kernel<true><<<nblk, ROWS, BLOCK_SMEM, st>>>(a);
       else block_kernel<false><<<nblk, ROWS, BLOCK_SMEM, st>>>(a);
       IC_CHECK_LAUNCH();
-      if (i2 < sbe) {  // near update inside the super-block (i1 % 4 == 0 here)
-        IC_TRY(gemm_tn(L.M, sbe - i2, i2 - i1, -1.f, e_hi + (i1 - sb), e_lo + (i1 - sb), lde,
-                       L.h_hi + i2 * L.ldh + i1, L.h_lo + i2 * L.ldh + i1, L.ldh, 1.f, L.W + i2, nullptr, L.ldw,
-                       L.W + i2, nullptr, L.ldw, L.passes, st));
-      }
     }
     if (sbe < L.N) {  // far update: everything after the super-block, K = super-block width
       const float* bh = L.h_hi + sbe * L.ldh + sb;
