@@ -41,6 +41,10 @@ from int_crush_converter_b200.sharding import max_over_ranks  # noqa: E402
 # (name, out_features, in_features) of one DiT linear set (config 3)
 LAYERS = [("qkv", 12288, 4096), ("proj", 4096, 4096), ("mlp_up", 16384, 4096), ("mlp_down", 4096, 16384)]
 PARAMS_PER_SET = sum(m * n for _, m, n in LAYERS)
+BLOCK_COLS = 128
+# algorithmic flop of one set: GPTQ trailing updates 2*M*N*(N-B) + the inverse N^3
+# (Cholesky, triangular inverse and U*U^T at N^3/3 each)
+FLOP_PER_SET = sum(2 * m * n * (n - BLOCK_COLS) + n ** 3 for _, m, n in LAYERS)
 N_SAMPLES = 8192
 ROT, BLOCK, DAMP = 256, 128, 0.01
 METRIC = "GPTQ-INT4 rot256 Mparams quantized/s"
@@ -280,6 +284,11 @@ def run_device(args, rank: int, world: int) -> None:
                                f"{gemm_ms:.2f} ms/launch",
                      "peak_basis": ("measured bf16 burst / 2 (TF32 rate) / 3 (3xTF32 products), of measured"
                                     if "bf16_tflops" in peaks else "fallback 1.59 PF bf16 / 2 / 3, of fallback")},
+        "step_roofline": {"bound": "tensor", "flop_per_step": FLOP_PER_SET,
+                          "target_ms": round(FLOP_PER_SET / (peak * 1e12) * 1e3, 3),
+                          "ms_per_step": round(ms_max / args.steps, 3),
+                          "frac": round(FLOP_PER_SET / (peak * 1e12) * 1e3 / (ms_max / args.steps), 4),
+                          "note": "whole step's algorithmic flop over the 3xTF32 peak, of measured"},
         "cpu_baseline": {"value": round(cpu_val, 4), "unit": "Mparams/s", "cores": cpu_cores(), "kind": "port",
                          "sample": "one proj layer [4096,4096] through oracle/cpu_ref.py (numpy + LAPACK)"},
         "clocks": clk.summary(),
