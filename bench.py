@@ -296,9 +296,9 @@ def run_device(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-# dram bytes (read + write) of one 16384^3 3xTF32 GEMM launch from the ncu capture summarised in
-# profiles/gemm_tn_3xtf32_16384.md (null until captured)
-TRAFFIC_BYTES = None
+# DRAM bytes (read + write) of the 16384^3 3xTF32 product timed by dominant_gemm_tflops (its four
+# K-slab launches together), from the ncu capture in profiles/gemm_tn_3xtf32_16384_traffic.md
+TRAFFIC_BYTES = 77_440_000_000
 
 
 def run_e2e(args, dev: torch.device, pool, world: int) -> dict:
