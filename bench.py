@@ -350,6 +350,82 @@ def run_e2e(args, dev: torch.device, pool, world: int) -> dict:
             "steps": steps, "api": "int_crush_converter_b200.LayerStreams.submit -> quantize_gptq_layer (C ABI ic_gptq_layer)"}
 
 
+def run_hbm_kernels(reps: int = 5) -> None:
+    """HBM-bound kernels of the path at the BASELINE configs' shapes, each timed
+    alone with CUDA events and reported against the measured copy bandwidth.
+    Algorithmic bytes (the minimum a kernel must move):
+      rtn_fused (config 1: fp16 W [4096,4096] x 8 layers, INT4 sym rot256):
+          2 B read + 0.5 B packed written per weight (+ 2 B scale per row)
+      rotate_weights (fp16 -> fp32 rot256, [4096,16384]): 2 B read + 4 B written per weight
+      rotate_hessian (fp32 H [16384,16384] -> rotated TF32 hi/lo pair, rot256):
+          4 B read + 8 B written per element"""
+    from int_crush_converter_b200 import _native as nat
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nat.require_device(dev)
+    lib = nat.load()
+    st = nat.stream_ptr(dev)
+    try:
+        peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]
+        basis = "of measured"
+    except (OSError, ValueError, KeyError):
+        peak, basis = 6650.0, "of fallback"
+    g = torch.Generator(device=dev).manual_seed(11)
+
+    def timed(fn, nbytes):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        return round(ms, 4), round(gbs, 1), round(gbs / peak, 4)
+
+    out = []
+    # config 1: RTN INT4 sym rot256 over 8 fp16 layers (256 MB of input, larger than L2)
+    Ws = [(torch.randn(4096, 4096, generator=g, device=dev) * 0.02).half() for _ in range(8)]
+    packed = torch.empty(4096, 2048, dtype=torch.uint8, device=dev)
+    sc = torch.empty(4096, dtype=torch.float16, device=dev)
+    sq = torch.empty(4096, dtype=torch.float64, device=dev)
+    mx = torch.empty(4096, dtype=torch.float32, device=dev)
+
+    def rtn():
+        for W in Ws:
+            nat.check(lib.ic_rtn_fused(W.data_ptr(), nat.IC_F16, 4096, 4096, 4096, 256, 4, 0, None, 0, None,
+                                       packed.data_ptr(), sc.data_ptr(), None, sq.data_ptr(), mx.data_ptr(), st))
+    ms, gbs, frac = timed(rtn, 8 * (4096 * 4096 * 2.5 + 4096 * 2))
+    out.append(dict(kernel="rtn_row_kernel (ic_rtn_fused)", workload="config 1: 8 x fp16 [4096,4096] INT4 sym rot256",
+                    ms_per_call=ms, achieved_gbs=gbs, frac=frac))
+    del Ws
+    W = (torch.randn(4096, 16384, generator=g, device=dev) * 0.02).half()
+    Wr = torch.empty(4096, 16384, device=dev)
+
+    def rot():
+        nat.check(lib.ic_rotate_weights(W.data_ptr(), nat.IC_F16, 4096, 16384, 16384, 256, Wr.data_ptr(), 16384, st))
+    ms, gbs, frac = timed(rot, 4096 * 16384 * 6)
+    out.append(dict(kernel="rotate_rows_kernel (ic_rotate_weights)", workload="fp16 [4096,16384] -> fp32, rot256",
+                    ms_per_call=ms, achieved_gbs=gbs, frac=frac))
+    del W, Wr
+    n = 16384
+    H = torch.randn(n, n, generator=g, device=dev)
+    hh = torch.empty(n, n, device=dev)
+    hl = torch.empty(n, n, device=dev)
+
+    def roth():
+        nat.check(lib.ic_rotate_hessian(H.data_ptr(), 1, n, n, 256, hh.data_ptr(), hl.data_ptr(), n, st))
+    ms, gbs, frac = timed(roth, n * n * 12)
+    out.append(dict(kernel="hess_rows_kernel + hess_cols_kernel (ic_rotate_hessian)",
+                    workload="fp32 H [16384,16384] -> hi/lo pair, rot256", ms_per_call=ms, achieved_gbs=gbs,
+                    frac=frac))
+    for o in out:
+        o.update(unit="GB/s", peak_gbs=peak, peak_basis=basis, bound="hbm")
+        print(json.dumps(o), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -361,7 +437,12 @@ def main() -> None:
     ap.add_argument("--streams", type=int, default=4, help="CUDA streams the layers are issued on")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="time only the dominant 3xTF32 GEMM at n^3 (small profiling case)")
+    ap.add_argument("--hbm-kernels", action="store_true",
+                    help="time the HBM-bound kernels (RTN, rotations) alone and exit")
     args = ap.parse_args()
+    if args.hbm_kernels:
+        run_hbm_kernels()
+        return
     if args.gemm_only:
         dev = torch.device("cuda", 0)
         tf, ms = dominant_gemm_tflops(dev, n=args.gemm_only, reps=2)

@@ -107,8 +107,32 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            _lib = lib
+            _lib = _Checked(lib)
     return _lib
+
+
+class _Checked:
+    """The loaded library with an argument-count check on every declared entry
+    point: ctypes forwards surplus arguments silently, and a pointer landing in
+    the wrong slot (a stream, a workspace) would reach the driver."""
+
+    def __init__(self, lib: ctypes.CDLL):
+        self._lib = lib
+        self._fns = {}
+        for name, (_, args) in SIGNATURES.items():
+            fn, n = getattr(lib, name), len(args)
+
+            def call(*a, _fn=fn, _n=n, _name=name):
+                if len(a) != _n:
+                    raise TypeError(f"{_name} takes {_n} arguments, got {len(a)}")
+                return _fn(*a)
+            self._fns[name] = call
+
+    def __getattr__(self, name):
+        fns = self.__dict__.get("_fns", {})
+        if name in fns:
+            return fns[name]
+        return getattr(self.__dict__["_lib"], name)
 
 
 def last_error() -> str:

@@ -16,19 +16,14 @@ template <typename T>
 __global__ void __launch_bounds__(256) rotate_rows_kernel(const T* __restrict__ W, int64_t N, int64_t ldw,
                                                           int rot, float* __restrict__ out, int64_t ldo,
                                                           int64_t npad) {
-  __shared__ float s[ROT_CHUNK];
+  __shared__ __align__(16) float s[ROT_CHUNK];
   const int64_t row = blockIdx.x;
   const int64_t c0 = (int64_t)blockIdx.y * ROT_CHUNK;
   const int len = (int)((npad - c0) < ROT_CHUNK ? (npad - c0) : ROT_CHUNK);
-  const T* src = W + row * ldw;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) {
-    const int64_t c = c0 + i;
-    s[i] = c < N ? load_as_f32(src + c) : 0.f;
-  }
+  load_row_smem(W + row * ldw, c0, N, len, s);
   __syncthreads();
-  hadamard_smem(s, len, rot, 1, 1, 0);
-  float* dst = out + row * ldo + c0;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) dst[i] = s[i];
+  hadamard_row(s, len, rot);
+  store_row_smem(s, len, out + row * ldo + c0);
 }
 
 // Row pass of R^T H R: every row of H gets the group Hadamard along its
@@ -36,20 +31,19 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const T* __restrict__ 
 __global__ void __launch_bounds__(256) hess_rows_kernel(const float* __restrict__ H, int64_t n, int64_t ldh,
                                                         int64_t bstride, int rot, float* __restrict__ out,
                                                         int64_t npad, int64_t ldo, int64_t ostride) {
-  __shared__ float s[ROT_CHUNK];
+  __shared__ __align__(16) float s[ROT_CHUNK];
   const int64_t row = blockIdx.x;
   const int64_t b = blockIdx.z;
   const int64_t c0 = (int64_t)blockIdx.y * ROT_CHUNK;
   const int len = (int)((npad - c0) < ROT_CHUNK ? (npad - c0) : ROT_CHUNK);
-  const float* src = H + b * bstride + row * ldh;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) {
-    const int64_t c = c0 + i;
-    s[i] = (row < n && c < n) ? src[c] : 0.f;
+  if (row < n) {
+    load_row_smem(H + b * bstride + row * ldh, c0, n, len, s);
+  } else {
+    for (int i = threadIdx.x; i < len; i += blockDim.x) s[i] = 0.f;
   }
   __syncthreads();
-  hadamard_smem(s, len, rot, 1, 1, 0);
-  float* dst = out + b * ostride + row * ldo + c0;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) dst[i] = s[i];
+  hadamard_row(s, len, rot);
+  store_row_smem(s, len, out + b * ostride + row * ldo + c0);
 }
 
 // Column pass: R^T along the row index within each group of `rot` rows, for a

@@ -173,21 +173,18 @@ __device__ void process_group(const float* x, int len, const RtnArgs& a, int64_t
 }
 
 __global__ void __launch_bounds__(NT) rtn_row_kernel(const RtnArgs a) {
-  extern __shared__ float row_s[];
+  extern __shared__ __align__(16) float row_s[];
   __shared__ float red[32];
   __shared__ double red_d[32];
   const int64_t row = blockIdx.x;
-  for (int64_t i = threadIdx.x; i < a.npad; i += NT) {
-    float v = 0.f;
-    if (i < a.N) {
-      if (a.dtype == IC_F16) v = __half2float(reinterpret_cast<const __half*>(a.W)[row * a.ldw + i]);
-      else if (a.dtype == IC_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.W)[row * a.ldw + i]);
-      else v = reinterpret_cast<const float*>(a.W)[row * a.ldw + i];
-    }
-    row_s[i] = v;
-  }
+  if (a.dtype == IC_F16)
+    load_row_smem(reinterpret_cast<const __half*>(a.W) + row * a.ldw, 0, a.N, (int)a.npad, row_s);
+  else if (a.dtype == IC_BF16)
+    load_row_smem(reinterpret_cast<const __nv_bfloat16*>(a.W) + row * a.ldw, 0, a.N, (int)a.npad, row_s);
+  else
+    load_row_smem(reinterpret_cast<const float*>(a.W) + row * a.ldw, 0, a.N, (int)a.npad, row_s);
   __syncthreads();
-  if (a.rot > 1) hadamard_smem(row_s, (int)a.npad, a.rot, 1, 1, 0);
+  if (a.rot > 1) hadamard_row(row_s, (int)a.npad, a.rot);
   double sq = 0.0;
   float mx = 0.f;
   if (a.G == 1) {

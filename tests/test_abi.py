@@ -30,3 +30,12 @@ def test_binding_covers_header():
 def test_version_and_no_device():
     lib = _native.load()
     assert b"sm_100a" in lib.ic_version()
+
+
+def test_binding_rejects_wrong_argument_count():
+    import pytest
+    lib = _native.load()
+    with pytest.raises(TypeError):
+        lib.ic_rotate_hessian(None, 1, 4, 4, 4, None, None, 4, 4, None)  # one too many
+    with pytest.raises(TypeError):
+        lib.ic_version(1)
