@@ -77,6 +77,54 @@ __global__ void __launch_bounds__(256) hess_cols_kernel(float* __restrict__ hi, 
   }
 }
 
+// Column pass for rot = 256 (radix 4, four digits of the row index within a
+// group), a strip of 32 columns per CTA of 512 threads, one column per lane.
+// Thread (w, c) first holds rows 16w + i (i = 0..15: digits 0 and 1) and
+// applies those two stages in registers; one transpose through shared memory
+// gives it rows w + 16j (j: digits 2 and 3) for the last two stages, which it
+// writes straight out (rows of a lane set stay column-coalesced).  Same
+// stage order and fp32 operations as hess_cols_kernel: bit-identical.
+constexpr int COLS_R = 32;
+__global__ void __launch_bounds__(512) hess_cols256_kernel(float* __restrict__ hi, float* __restrict__ lo,
+                                                           int64_t npad, int64_t ldo, int64_t ostride) {
+  __shared__ float tile[256][COLS_R + 1];
+  const int c = threadIdx.x & 31, w = threadIdx.x >> 5;  // w = 0..15
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * 256;
+  const int64_t col = (int64_t)blockIdx.x * COLS_R + c;
+  const bool cv = col < npad;
+  float* base = hi + b * ostride + r0 * ldo + col;
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = cv ? base[(int64_t)(16 * w + i) * ldo] : 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);  // digit 0
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4(v[q], v[4 + q], v[8 + q], v[12 + q]);  // digit 1
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tile[16 * w + i][c] = v[i];
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = tile[w + 16 * j][c];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);  // digit 2
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4(v[q], v[4 + q], v[8 + q], v[12 + q]);  // digit 3
+  if (!cv) return;
+  float* lbase = lo ? lo + b * ostride + r0 * ldo + col : nullptr;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int64_t o = (int64_t)(w + 16 * j) * ldo;
+    if (lbase) {
+      const float h = to_tf32(v[j]);
+      base[o] = h;
+      lbase[o] = __fsub_rn(v[j], h);
+    } else {
+      base[o] = v[j];
+    }
+  }
+}
+
 __global__ void split_kernel(const float* __restrict__ in, int64_t rows, int64_t cols, int64_t ldi,
                              float* __restrict__ hi, float* __restrict__ lo, int64_t ldo) {
   const int64_t total = rows * cols;
@@ -130,7 +178,11 @@ int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int r
   dim3 g1((unsigned)npad, (unsigned)cdiv(npad, ROT_CHUNK), (unsigned)nbatch);
   hess_rows_kernel<<<g1, 256, 0, st>>>(H, n, ldh, n * ldh, r, out_hi, npad, ldo, ostride);
   IC_CHECK_LAUNCH();
-  if (r > 1) {
+  if (r == 256) {
+    dim3 g2((unsigned)cdiv(npad, COLS_R), (unsigned)(npad / 256), (unsigned)nbatch);
+    hess_cols256_kernel<<<g2, 512, 0, st>>>(out_hi, out_lo, npad, ldo, ostride);
+    IC_CHECK_LAUNCH();
+  } else if (r > 1) {
     const size_t sm = (size_t)r * (COLS + 1) * 4;
     if (sm > 48 * 1024)
       IC_CUDA(cudaFuncSetAttribute(hess_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
