@@ -152,13 +152,42 @@ __device__ __forceinline__ void cross2(float (&v)[16], int m, bool upper) {
   }
 }
 
+// The group Hadamard of 16 consecutive elements per lane, L = rot/16 lanes per
+// group (lane l of the group holds elements 16l .. 16l+15), all lanes of the
+// warp taking part (shfl_xor).  16 <= rot <= 512.
+__device__ __forceinline__ void hadamard_regs16(float (&v)[16], int rot, int l) {
+  const int L = rot / 16;
+  const bool p4 = is_pow4(rot);
+  if (p4) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) h4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) h4(v[q], v[4 + q], v[8 + q], v[12 + q]);
+    for (int m = 1; m < L; m <<= 2) cross4(v, m);
+  } else {
+#pragma unroll
+    for (int st = 1; st < 16; st <<= 1) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j & st) continue;
+        const float a0 = v[j], a1 = v[j + st];
+        v[j] = __fadd_rn(a0, a1);
+        v[j + st] = __fsub_rn(a0, a1);
+      }
+    }
+    for (int m = 1; m < L; m <<= 1) cross2(v, m, (l & m) != 0);
+    const float c = (float)(1.0 / sqrt((double)rot));  // fp32(1/sqrt(n)), rotation.py:36
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], c);
+  }
+}
+
 __device__ inline void hadamard_row_regs(float* s, int len, int rot) {
   const int L = rot / 16;      // lanes per group
   const int gpw = 32 / L;      // groups per warp pass
   const int ngroups = len / rot;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int l = lane & (L - 1);
-  const bool p4 = is_pow4(rot);
   for (int g0 = warp * gpw; g0 < ngroups; g0 += nw * gpw) {
     const int g = g0 + lane / L;
     const bool act = g < ngroups;
@@ -172,28 +201,7 @@ __device__ inline void hadamard_row_regs(float* s, int len, int rot) {
       v[4 * q + 2] = t.z;
       v[4 * q + 3] = t.w;
     }
-    if (p4) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) h4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) h4(v[q], v[4 + q], v[8 + q], v[12 + q]);
-      for (int m = 1; m < L; m <<= 2) cross4(v, m);
-    } else {
-#pragma unroll
-      for (int st = 1; st < 16; st <<= 1) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j & st) continue;
-          const float a0 = v[j], a1 = v[j + st];
-          v[j] = __fadd_rn(a0, a1);
-          v[j + st] = __fsub_rn(a0, a1);
-        }
-      }
-      for (int m = 1; m < L; m <<= 1) cross2(v, m, (l & m) != 0);
-      const float c = (float)(1.0 / sqrt((double)rot));  // fp32(1/sqrt(n)), rotation.py:36
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], c);
-    }
+    hadamard_regs16(v, rot, l);
     if (act) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) p[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);

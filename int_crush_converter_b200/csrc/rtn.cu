@@ -217,6 +217,228 @@ __global__ void __launch_bounds__(NT) rtn_row_kernel(const RtnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Register-only path for a per-row scale (G == 1), 16 <= rot <= 512 (or no
+// rotation), npad <= 16 * NT: one CTA per row, lane ch of the CTA owns
+// elements 16ch .. 16ch+15 of the row in registers from the load to the
+// stores (no shared-memory copy of the row).  The XU pipe (reciprocal,
+// conversions, floor) bounded the shared-memory kernel, so the per-element
+// work here is ALU/FMA only:
+//   * x / s through RN(1/s) with one FMA correction; a quotient that lands
+//     within a few ulps of a rounding boundary of the code is recomputed with
+//     the IEEE division, so the codes equal the shared-memory kernel's;
+//   * round-half-away with an exact magic-number floor (|y| < 2^22);
+//   * verify statistics as fp32 partial sums per lane (16 terms), fp64 across.
+// The clip-ratio search keeps the IEEE division and round-half-even of the
+// reference (its candidate MSEs decide the scale).
+__device__ __forceinline__ float floor_small(float y) {  // 0 <= y < 2^22
+  const float r = __fsub_rn(__fadd_rn(y, 8388608.f), 8388608.f);  // RN(y)
+  return r > y ? __fsub_rn(r, 1.f) : r;
+}
+__device__ __forceinline__ float rhaz_fast(float x) {
+  const float a = fabsf(x);
+  if (!(a < 4194304.f)) return rhaz(x);  // large or NaN
+  return copysignf(floor_small(__fadd_rn(a, 0.5f)), x);
+}
+// v / s rounded as __fdiv_rn(v, s) wherever it can change the code
+__device__ __forceinline__ float code_arg(float v, float s, float rs, float z, bool has_z) {
+  const float q0 = __fmul_rn(v, rs);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, s, v), rs, q0);
+  float y = has_z ? __fadd_rn(q, z) : q;
+  const float a = fabsf(y);
+  if (a < 64.f) {
+    const float t = __fadd_rn(a, 0.5f);
+    const float d = __fsub_rn(t, floor_small(t));
+    if (d < 0x1p-14f || d > 1.f - 0x1p-14f) {
+      y = __fdiv_rn(v, s);
+      if (has_z) y = __fadd_rn(y, z);
+    }
+  }
+  return y;
+}
+
+// two's-complement bits of an integer-valued float in [-2^22, 2^22] without
+// the conversion unit: x + 1.5*2^23 holds x in its low mantissa bits
+__device__ __forceinline__ uint32_t small_int_bits(float x) {
+  return (uint32_t)__float_as_int(__fadd_rn(x, 12582912.f)) - 0x4B400000u;
+}
+
+template <typename Op>
+__device__ __forceinline__ float cta_reduce(float v, Op op, float* red) {
+  for (int o = 16; o; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = op(r, red[w]);
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT) rtn_regs_kernel(const RtnArgs a) {
+  __shared__ float red[32];
+  __shared__ double red_d[32];
+  const int64_t row = blockIdx.x;
+  const int ch = threadIdx.x;
+  const int64_t c0 = (int64_t)ch * 16;
+  const bool act = c0 < a.npad;
+  const float qmin = a.bits == 4 ? -8.f : -128.f;
+  const float qmax = a.bits == 4 ? 7.f : 127.f;
+
+  float v[16];
+  const T* src = reinterpret_cast<const T*>(a.W) + row * a.ldw + c0;
+  constexpr int V = 16 / sizeof(T);
+  if (act && c0 + 16 <= a.N && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 16 / V; ++q) {
+      const uint4 raw = reinterpret_cast<const uint4*>(src)[q];
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int u = 0; u < V; ++u) v[q * V + u] = load_as_f32(e + u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = (act && c0 + j < a.N) ? load_as_f32(src + j) : 0.f;
+  }
+  if (a.rot > 1) hadamard_regs16(v, a.rot, ch & (a.rot / 16 - 1));
+
+  // ---- per-row scale (converter/scales.py, as process_group) ----
+  float s = 0.f, zp = 0.f;
+  {
+    float amax = 0.f, wmin = __int_as_float(0x7f800000), wmax = __int_as_float(0xff800000);
+    if (act) {
+      if (a.asym) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          wmin = nmin(wmin, v[j]);
+          wmax = nmax(wmax, v[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) amax = nmax(amax, fabsf(v[j]));
+      }
+    }
+    if (a.asym) {
+      wmin = cta_reduce(wmin, OpMin(), red);
+      wmax = cta_reduce(wmax, OpMax(), red);
+    } else {
+      amax = cta_reduce(amax, OpMax(), red);
+    }
+    const float div = a.asym ? (qmax - qmin) : (a.bits == 4 ? 7.f : 127.f);
+    if (a.nratios == 0) {
+      if (a.asym) {
+        s = clamp_scale(__fdiv_rn(__fsub_rn(wmax, wmin), div));
+        s = fix_asym(s, wmin, wmax, qmin, qmax);
+        zp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, s))), qmin, qmax);
+        if (a.zero_group_zp0 && wmin == 0.f && wmax == 0.f) zp = 0.f;
+      } else {
+        s = clamp_scale(__fdiv_rn(amax, div));
+      }
+    } else {
+      float best_mse = 0.f;
+      for (int r = 0; r < a.nratios; ++r) {
+        const float ratio = a.ratios[r];
+        float cs, czp = 0.f;
+        if (a.asym) {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(__fsub_rn(wmax, wmin), ratio), div));
+          cs = fix_asym(cs, wmin, wmax, qmin, qmax);
+          czp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, cs))), qmin, qmax);
+        } else {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(amax, ratio), div));
+        }
+        float part = 0.f;
+        if (act) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float y = __fdiv_rn(v[j], cs);
+            if (a.asym) y = __fadd_rn(y, czp);
+            const float q = clampf(rintf(y), qmin, qmax);
+            const float deq = a.asym ? __fmul_rn(__fsub_rn(q, czp), cs) : __fmul_rn(q, cs);
+            const float e = __fsub_rn(v[j], deq);
+            part = __fadd_rn(part, __fmul_rn(e, e));
+          }
+        }
+        const float mse = __fdiv_rn(cta_reduce(part, OpSum(), red), (float)a.npad);
+        if (r == 0 || mse < best_mse) {
+          best_mse = mse;
+          s = cs;
+          zp = czp;
+        }
+      }
+    }
+  }
+  const uint16_t s16 = __half_as_ushort(__float2half_rn(s));
+  if (threadIdx.x == 0) {
+    if (a.scales) a.scales[row] = s16;
+    if (a.zp && a.asym) a.zp[row] = (int8_t)zp;
+  }
+
+  // ---- codes, packing, verify statistics ----
+  const float sf = __half2float(__ushort_as_half(s16));
+  const float rs = __frcp_rn(sf);
+  float part = 0.f, mx = 0.f;
+  float q[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    q[j] = clampf(rhaz_fast(code_arg(v[j], sf, rs, zp, a.asym != 0)), qmin, qmax);
+    const float deq = a.asym ? __fmul_rn(__fsub_rn(q[j], zp), sf) : __fmul_rn(q[j], sf);
+    const float d = __fsub_rn(v[j], deq);
+    part = __fmaf_rn(d, d, part);
+    mx = nmax(mx, fabsf(d));
+  }
+  if (act) {
+    if (a.codes) {
+      int8_t* dst = a.codes + row * a.ldc + c0;
+      uint32_t w4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        w4[i] = (small_int_bits(q[4 * i]) & 255u) | ((small_int_bits(q[4 * i + 1]) & 255u) << 8) |
+                ((small_int_bits(q[4 * i + 2]) & 255u) << 16) | ((small_int_bits(q[4 * i + 3]) & 255u) << 24);
+      if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dst[j] = (int8_t)q[j];
+      }
+    }
+    if (a.packed) {
+      uint8_t* dst = a.packed + row * a.ldp + c0 / 2;
+      uint32_t p2[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) p2[j >> 3] |= (small_int_bits(q[j]) & 15u) << (4 * (j & 7));
+      if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(p2[0], p2[1]);
+      } else {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) dst[b] = (uint8_t)(p2[b >> 2] >> (8 * (b & 3)));
+      }
+    }
+  } else {
+    part = 0.f;
+    mx = 0.f;
+  }
+  if (a.row_sqerr || a.row_maxerr) {
+    double sq = warp_sum_d((double)part);
+    for (int o = 16; o; o >>= 1) mx = nmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+      red_d[threadIdx.x >> 5] = sq;
+      red[threadIdx.x >> 5] = mx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      float m = 0.f;
+      for (int w = 0; w < NT / 32; ++w) {
+        t += red_d[w];
+        m = nmax(m, red[w]);
+      }
+      if (a.row_sqerr) a.row_sqerr[row] = t;
+      if (a.row_maxerr) a.row_maxerr[row] = m;
+    }
+  }
+}
+
 __global__ void pack_kernel(const int8_t* __restrict__ codes, int64_t M, int64_t K, int64_t ldc,
                             uint8_t* __restrict__ packed, int64_t ldp, unsigned* flags) {
   const int64_t kp = (K + 1) / 2;
@@ -245,6 +467,16 @@ __global__ void unpack_kernel(const uint8_t* __restrict__ packed, int64_t M, int
 
 int launch_rtn(RtnArgs& a, int64_t M, cudaStream_t st) {
   if (M == 0 || a.npad == 0) return IC_OK;
+  if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rtn: too many rows");
+  if (a.G == 1 && !a.given && a.npad <= 16 * NT && a.npad % 16 == 0 && (a.rot <= 1 || hadamard_regs_ok(a.rot))) {
+    switch (a.dtype) {
+      case IC_F16: rtn_regs_kernel<__half><<<(unsigned)M, NT, 0, st>>>(a); break;
+      case IC_BF16: rtn_regs_kernel<__nv_bfloat16><<<(unsigned)M, NT, 0, st>>>(a); break;
+      default: rtn_regs_kernel<float><<<(unsigned)M, NT, 0, st>>>(a); break;
+    }
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
   if (a.npad > MAX_ROW)
     return fail(IC_ERR_UNSUPPORTED, "rtn: row of %lld elements exceeds %lld", (long long)a.npad, (long long)MAX_ROW);
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rtn: too many rows");
