@@ -59,12 +59,23 @@ struct BlockArgs {
   int vec;  // W and Hinv rows of this block are 16-byte aligned
 };
 
+// Compact Hinv block: row j keeps columns [32*(j/32), 128) only (the serial
+// part reads its group's diagonal block, the apply part the columns after it).
+constexpr int HS_FLOATS = GROUP * (MAXB + (MAXB - GROUP) + (MAXB - 2 * GROUP) + (MAXB - 3 * GROUP));
+__device__ __forceinline__ int hs_index(int j, int c) {
+  const int G = j >> 5;
+  const int base = GROUP * (MAXB * G - 16 * G * (G - 1));  // sum of the earlier groups' rows
+  return base + (j - G * GROUP) * (MAXB - G * GROUP) + (c - G * GROUP);
+}
+
 template <bool LDLQ>
 __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
   extern __shared__ float smem[];
-  float* hs = smem;                // [MAXB][MAXB] Hinv block (exact fp32), row j = error column j
-  float* wsm = hs + MAXB * MAXB;   // [MAXB][ROWS] this CTA's weights of the block, column-major
-  float* dinv = wsm + MAXB * ROWS;  // [MAXB] LDLQ: 1/max(Hinv[j,j],1e-8)
+  // Hinv block (exact fp32), row j = error column j, compact: only columns from
+  // the start of row j's group on are ever read (HS_FLOATS = 32 x (128+96+64+32))
+  float* hs = smem;
+  float* wsm = hs + HS_FLOATS;      // [MAXB-GROUP][ROWS] weights of groups 1..3, column-major
+  float* dinv = wsm + (MAXB - GROUP) * ROWS;  // [MAXB] LDLQ: 1/max(Hinv[j,j],1e-8)
 
   const int t = threadIdx.x;
   const int bc = a.bc;
@@ -90,21 +101,22 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
       for (int u = 0; u < 8; ++u) {
         const int idx = (it + u) * ROWS + t;
         const int j = idx >> 5, k4 = (idx & 31) << 2;
-        *reinterpret_cast<float4*>(hs + j * MAXB + k4) =
-            make_float4(__fadd_rn(hv[u].x, lv[u].x), __fadd_rn(hv[u].y, lv[u].y), __fadd_rn(hv[u].z, lv[u].z),
-                        __fadd_rn(hv[u].w, lv[u].w));
+        if (k4 >= (j & ~(GROUP - 1)))
+          *reinterpret_cast<float4*>(hs + hs_index(j, k4)) =
+              make_float4(__fadd_rn(hv[u].x, lv[u].x), __fadd_rn(hv[u].y, lv[u].y),
+                          __fadd_rn(hv[u].z, lv[u].z), __fadd_rn(hv[u].w, lv[u].w));
       }
     }
-    // this row's 128 weights, 8 float4 loads in flight
+    // this row's weights of groups 1..3 (group 0 goes to registers later), 8 float4 loads in flight
     const float4* wrow = reinterpret_cast<const float4*>(a.W + rr * a.ldw + a.i1);
 #pragma unroll 1
-    for (int c4 = 0; c4 < MAXB / 4; c4 += 8) {
+    for (int c4 = GROUP / 4; c4 < MAXB / 4; c4 += 8) {
       float4 v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) v[u] = wrow[c4 + u];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int c = 4 * (c4 + u);
+        const int c = 4 * (c4 + u) - GROUP;
         wsm[c * ROWS + t] = v[u].x;
         wsm[(c + 1) * ROWS + t] = v[u].y;
         wsm[(c + 2) * ROWS + t] = v[u].z;
@@ -113,16 +125,16 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
     }
   } else {
     for (int j = 0; j < bc; ++j)
-      for (int k = t; k < bc; k += ROWS) {
+      for (int k = (j & ~(GROUP - 1)) + t; k < bc; k += ROWS) {
         const int64_t o = (a.i1 + j) * a.ldh + a.i1 + k;
-        hs[j * MAXB + k] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
+        hs[hs_index(j, k)] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
       }
     const float* wrow = a.W + rr * a.ldw + a.i1;
-    for (int c = 0; c < bc; ++c) wsm[c * ROWS + t] = wrow[c];
+    for (int c = GROUP; c < bc; ++c) wsm[(c - GROUP) * ROWS + t] = wrow[c];
   }
   __syncthreads();
   if (LDLQ)
-    for (int j = t; j < bc; j += ROWS) dinv[j] = __fdiv_rn(1.0f, fmaxf(hs[j * MAXB + j], 1e-8f));
+    for (int j = t; j < bc; j += ROWS) dinv[j] = __fdiv_rn(1.0f, fmaxf(hs[hs_index(j, j)], 1e-8f));
   if (LDLQ) __syncthreads();
 
   const float s = LDLQ ? 1.f : a.scale[rr];
@@ -137,11 +149,29 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
 #pragma unroll 1
   for (int G = 0; G < ng; ++G) {
     const int cb = G * GROUP;  // first block-local column of the group
+    const float* hg = hs + hs_index(cb, cb);  // row cb of the group's compact rows, stride hstride
+    const int hstride = MAXB - cb;
     float w[GROUP], ev[GROUP];
     float sc[LDLQ ? GROUP : 1];
+    if (G == 0) {
+      const float* wrow = a.W + rr * a.ldw + a.i1;
+      if (a.vec && bc >= GROUP) {
+#pragma unroll
+        for (int c4 = 0; c4 < GROUP / 4; ++c4) {
+          const float4 q4 = reinterpret_cast<const float4*>(wrow)[c4];
+          w[4 * c4] = q4.x;
+          w[4 * c4 + 1] = q4.y;
+          w[4 * c4 + 2] = q4.z;
+          w[4 * c4 + 3] = q4.w;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < GROUP; ++c) w[c] = (c < bc) ? wrow[c] : 0.f;
+      }
+    }
 #pragma unroll
     for (int c = 0; c < GROUP; ++c) {
-      w[c] = (cb + c < bc) ? wsm[(cb + c) * ROWS + t] : 0.f;
+      if (G > 0) w[c] = (cb + c < bc) ? wsm[(cb + c - GROUP) * ROWS + t] : 0.f;
       if (LDLQ) sc[c] = (cb + c < bc) ? fmaxf(a.scale2d[rr * a.lds + a.i1 + cb + c], 1e-8f) : 1.f;
     }
     // the group's columns in order, each error applied at once to the group's later columns
@@ -157,7 +187,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
           if (has_zp) raw = __fadd_rn(raw, z);
           q = clampf(rhaz(raw), a.qmin, a.qmax);
           const float deq = has_zp ? __fmul_rn(__fsub_rn(q, z), s) : __fmul_rn(q, s);
-          e = __fdiv_rn(__fsub_rn(x, deq), hs[j * MAXB + j]);
+          e = __fdiv_rn(__fsub_rn(x, deq), hg[c * hstride + c]);
           e = clampf(e, -100.f, 100.f);  // ERR_CLAMP_RANGE
           if (e != e) e = 0.f;           // nan_to_num
         } else {
@@ -178,7 +208,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
         ev[c] = e;
 #pragma unroll 31
         for (int c2 = c + 1; c2 < GROUP; ++c2)
-          if (cb + c2 < bc) w[c2] = __fsub_rn(w[c2], __fmul_rn(e, hs[j * MAXB + cb + c2]));
+          if (cb + c2 < bc) w[c2] = __fsub_rn(w[c2], __fmul_rn(e, hg[c * hstride + c2]));
       }
     }
 
@@ -268,20 +298,20 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
     const int cend = (bc + 3) & ~3;  // columns past bc are scratch (never read back)
 #pragma unroll 1
     for (int c2 = cb + GROUP; c2 < cend; c2 += 4) {
-      float v0 = wsm[c2 * ROWS + t], v1 = wsm[(c2 + 1) * ROWS + t];
-      float v2 = wsm[(c2 + 2) * ROWS + t], v3 = wsm[(c2 + 3) * ROWS + t];
+      float* wc = wsm + (c2 - GROUP) * ROWS + t;
+      float v0 = wc[0], v1 = wc[ROWS], v2 = wc[2 * ROWS], v3 = wc[3 * ROWS];
 #pragma unroll
       for (int j = 0; j < GROUP; ++j) {
-        const float4 h = *reinterpret_cast<const float4*>(hs + (cb + j) * MAXB + c2);
+        const float4 h = *reinterpret_cast<const float4*>(hg + j * hstride + (c2 - cb));
         v0 = __fsub_rn(v0, __fmul_rn(ev[j], h.x));
         v1 = __fsub_rn(v1, __fmul_rn(ev[j], h.y));
         v2 = __fsub_rn(v2, __fmul_rn(ev[j], h.z));
         v3 = __fsub_rn(v3, __fmul_rn(ev[j], h.w));
       }
-      wsm[c2 * ROWS + t] = v0;
-      wsm[(c2 + 1) * ROWS + t] = v1;
-      wsm[(c2 + 2) * ROWS + t] = v2;
-      wsm[(c2 + 3) * ROWS + t] = v3;
+      wc[0] = v0;
+      wc[ROWS] = v1;
+      wc[2 * ROWS] = v2;
+      wc[3 * ROWS] = v3;
     }
   }
   if (want_stats && rv) {
@@ -290,7 +320,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
   }
 }
 
-constexpr size_t BLOCK_SMEM = (size_t)MAXB * MAXB * 4 + (size_t)MAXB * ROWS * 4 + MAXB * 4;
+constexpr size_t BLOCK_SMEM = (size_t)HS_FLOATS * 4 + (size_t)(MAXB - GROUP) * ROWS * 4 + MAXB * 4;
 
 // ---- per-row scale / zero-point preparation (converter/gptq.py:254-317) ----
 __global__ void __launch_bounds__(256) row_params_kernel(const float* __restrict__ W, int64_t N, int64_t ldw,
