@@ -273,7 +273,7 @@ def run_device(args, rank: int, world: int) -> None:
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 inverse; TF32 products with fp32 accumulation for the GPTQ trailing update)", "data": "synthetic",
         "config": dict(CONFIG, parallelism=f"layer sets sharded over {world} GPU(s), no collective",
                        streams=args.streams),
         "e2e": e2e,

@@ -197,11 +197,15 @@ int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw
  * verify statistics and the layer's status bits, 2 = Hessian not positive
  * definite) the call does not synchronise and the caller checks stats[2]
  * (the reference then takes its inv/pinv branch); with stats == NULL it
- * synchronises once and returns IC_ERR_NOT_PD. */
+ * synchronises once and returns IC_ERR_NOT_PD.  update_passes: the lazy
+ * trailing update W -= E * Hinv (rounding.py:100-103) as 1 = TF32 products
+ * with fp32 accumulation or 3 = 3xTF32 (fp32-class); the Hessian inverse is
+ * always 3xTF32.  Both keep tr((W-Q)H(W-Q)^T) within 0.15% of the reference
+ * on the parity aggregates; 1 does a third of the update's tensor work. */
 size_t ic_gptq_layer_workspace_size(int64_t M, int64_t N_in, int rot);
 int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, int64_t ldw, const float* H,
                   int64_t ldh, int h_rotated, int rot, int bits, int asym, int block_size,
-                  float damping, int8_t* codes, uint8_t* packed, uint16_t* scales_f16,
+                  float damping, int update_passes, int8_t* codes, uint8_t* packed, uint16_t* scales_f16,
                   int8_t* zp, double* stats, void* workspace, size_t workspace_bytes,
                   void* stream);
 

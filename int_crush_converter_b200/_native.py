@@ -65,7 +65,7 @@ SIGNATURES = {
                                    _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _vp]),
     "ic_gptq_layer_workspace_size": (_sz, [_i64, _i64, _i32]),
     "ic_gptq_layer": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32,
-                             _f32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+                             _f32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ic_ldlq_run": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _i64, _i32, _i32,
                            _vp, _i64, _i32, _vp, _sz, _vp]),
     "ic_ldlq_update_scales": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _vp]),

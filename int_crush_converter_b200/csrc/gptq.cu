@@ -671,10 +671,12 @@ extern "C" size_t ic_gptq_layer_workspace_size(int64_t M, int64_t N_in, int rot)
 
 extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, int64_t ldw_in, const float* H,
                              int64_t ldh_in, int h_rotated, int rot, int bits, int asym, int block_size, float damping,
+                             int update_passes,
                              int8_t* codes, uint8_t* packed, uint16_t* scales_f16, int8_t* zp_out, double* stats,
                              void* workspace, size_t workspace_bytes, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   if (bits != 4 && bits != 8) return fail(IC_ERR_INVALID, "int_bits must be 4 or 8, got %d", bits);
+  if (update_passes != 1 && update_passes != 3) return fail(IC_ERR_INVALID, "update_passes must be 1 or 3");
   if (block_size <= 0 || block_size > MAXB) return fail(IC_ERR_UNSUPPORTED, "block_size must be in [1,%d]", MAXB);
   if (bits == 4 && packed && block_size % 2) return fail(IC_ERR_UNSUPPORTED, "gptq_layer: odd block size with packing");
   const int r = rot > 0 ? rot : 1;
@@ -707,7 +709,7 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   L.scale = w.scale; L.zp = has_zp ? w.zp : nullptr; L.stat_scale = w.sscale;
   L.qmin = bits == 4 ? -8 : -128; L.qmax = bits == 4 ? 7 : 127;
   L.codes = codes; L.ldq = npad; L.packed = bits == 4 ? packed : nullptr;
-  L.ldp = (npad + 1) / 2; L.row_sqerr = w.rsq; L.row_maxerr = w.rmx; L.passes = 3; L.ldlq = false;
+  L.ldp = (npad + 1) / 2; L.row_sqerr = w.rsq; L.row_maxerr = w.rmx; L.passes = update_passes; L.ldlq = false;
   IC_TRY(run_loop(L, w.loop, w.loop_bytes, st));
   if (stats) {
     stats_kernel<<<1, 1024, 0, st>>>(w.rsq, w.rmx, M, (double)M * (double)npad, stats, w.status);

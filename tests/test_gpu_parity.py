@@ -323,17 +323,19 @@ def test_gptq_block_size_not_multiple_of_4():
     assert abs(p / pr - 1) < 0.02
 
 
-def test_gptq_aggregate_proxy_vs_oracle():
-    """Several mid-size layers: sum of tr(E H E^T) within 0.5% of the oracle's."""
+@pytest.mark.parametrize("update_passes,M,N,layers", [(1, 256, 1024, 4), (3, 256, 1024, 4), (1, 512, 2048, 2)])
+def test_gptq_aggregate_proxy_vs_oracle(update_passes, M, N, layers):
+    """Several mid-size layers: sum of tr(E H E^T) within 0.5% of the oracle's,
+    for both precisions of the trailing update."""
     tot_gpu = tot_ref = 0.0
-    for seed in range(4):
-        M, N = 256, 1024
+    for seed in range(layers):
         W = gi.weight_outlier_cols(100 + seed, M, N)
-        H = gi.hessian_lognormal(200 + seed, N, 2048)
+        H = gi.hessian_lognormal(200 + seed, N, 2 * N)
         Wr = R.rotate_weights(W, 256)
         Hr = R.rotate_hessian(H, 256)
         ref = R.gptq_quantize_layer(Wr, Hr, 128, 0.01, 4)
-        out = B.quantize_gptq_layer(cu(W).half(), cu(H), rot_size=256, want_codes=True)
+        out = B.quantize_gptq_layer(cu(W).half(), cu(H), rot_size=256, want_codes=True,
+                                    update_passes=update_passes)
         q = np_(out["codes"])
         assert np.array_equal(np_(out["scales"]), ref["scales"])
         assert np.array_equal(np_(B.unpack_int4(out["packed"], N)), q)
@@ -359,7 +361,7 @@ def test_gptq_layer_not_pd_reported():
     packed = torch.empty(M, N // 2, dtype=torch.uint8, device="cuda")
     s16 = torch.empty(M, dtype=torch.float16, device="cuda")
     zp = torch.empty(M, dtype=torch.int8, device="cuda")
-    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, 0, 256, 4, 0, 128, 0.01, None,
+    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, 0, 256, 4, 0, 128, 0.01, 1, None,
                            packed.data_ptr(), s16.data_ptr(), zp.data_ptr(), None, ws.data_ptr(), ws.numel(),
                            nat.stream_ptr(W.device))
     assert st == nat.IC_ERR_NOT_PD
