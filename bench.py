@@ -439,7 +439,21 @@ def main() -> None:
                     help="time only the dominant 3xTF32 GEMM at n^3 (small profiling case)")
     ap.add_argument("--hbm-kernels", action="store_true",
                     help="time the HBM-bound kernels (RTN, rotations) alone and exit")
+    ap.add_argument("--one-step", action="store_true",
+                    help="quantize one set once and exit (for an ncu launch list of exactly one step)")
     args = ap.parse_args()
+    if args.one_step:
+        import int_crush_converter_b200 as B
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        s = make_set(0, dev)
+        torch.cuda.synchronize(dev)
+        with B.LayerStreams(args.streams, dev) as pool:
+            for _, W, H in s:
+                pool.submit(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"one_step": "ok", "layers": len(s)}))
+        return
     if args.hbm_kernels:
         run_hbm_kernels()
         return
