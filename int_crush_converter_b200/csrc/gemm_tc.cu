@@ -36,6 +36,8 @@ struct GemmArgs {
   long long ldd;
   unsigned* flags;
   int vec;  // C/D rows 16-byte aligned: vectorised epilogue
+  int group;  // row-tiles per group of the tile order
+  int chunk;  // k-tiles per TMEM accumulator chunk (3xTF32)
   int kofs;  // K index of column 0 of A/B in the full product (K-slab launches)
   int tri;  // bit 0: only output tiles on/below the diagonal (n0 <= m0);
             // bit 1: A rows are zero left of their own index (upper triangular
@@ -296,12 +298,11 @@ struct Cfg {
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (PASSES == 3 ? 2 : 1);
   static constexpr int STAGES = 196608 / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  // 3xTF32: K is accumulated in chunks of CHUNK k-tiles into two alternating
+  // 3xTF32: K is accumulated in chunks of `chunk` k-tiles (default 4) into a ring of
   // TMEM accumulators; the epilogue adds the chunks in fp32 registers with
   // round-to-nearest.  The tensor core's own fp32 accumulation truncates, and
-  // over a long K its bias adds up; chunking bounds that to CHUNK*32 terms.
+  // over a long K its bias adds up; chunking bounds that to chunk*32 terms.
   static constexpr bool CHUNKED = PASSES == 3;
-  static constexpr int CHUNK = 2;
   static constexpr int NACC = CHUNKED ? 4 : 1;  // ring of accumulators: the epilogue may lag NACC-1 chunks
   static constexpr int TMEM_COLS = NACC * BN;
   static_assert(4 * 32 * EPI_LD * 4 <= STAGES * STAGE_BYTES, "epilogue staging fits in the stages");
@@ -314,7 +315,7 @@ __global__ void __launch_bounds__(384, 1)
                    const GemmArgs args) {
   using C = Cfg<BN, PASSES>;
   constexpr int STAGES = C::STAGES;
-  constexpr int CH = C::CHUNKED ? C::CHUNK : (1 << 30);
+  const int CH = C::CHUNKED ? args.chunk : (1 << 30);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(384, 1)
   bool ok = true;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     int tm, tn;
-    tile_of(tile, mt, nt, GROUP_M, tm, tn);
+    tile_of(tile, mt, nt, args.group, tm, tn);
     const int m0 = tm * BM;
     const int n0 = tn * BN;
     if ((args.tri & 1) && n0 > m0) continue;  // strictly-upper tile of a symmetric/lower result
@@ -810,6 +811,26 @@ int gemm_prepare() {
 }
 
 namespace {
+// Tile-order group height and accumulator chunk length (IC_GEMM_GROUP,
+// IC_GEMM_CHUNK override the defaults for tuning).  Measured on B200: chunks of
+// 4 k-tiles (128 K) were 2-4% faster in the bench than 2 and keep the inverse
+// within 8x LAPACK's error; 8 exceeded that bound.  Group heights 8 and 16
+// tie; 32 is slower at 16384^3.
+int tune_group() {
+  static const int v = [] {
+    const char* e = getenv("IC_GEMM_GROUP");
+    return (e && atoi(e) > 0) ? atoi(e) : GROUP_M;
+  }();
+  return v;
+}
+int tune_chunk() {
+  static const int v = [] {
+    const char* e = getenv("IC_GEMM_CHUNK");
+    return (e && atoi(e) > 0) ? atoi(e) : 4;
+  }();
+  return v;
+}
+
 int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
               int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
               const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
@@ -827,7 +848,7 @@ int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, c
   unsigned* flags = device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
   GemmArgs a{(int)m, (int)n, (int)(k > 0 ? k : 0), alpha, beta, c_hi, c_lo, (long long)ldc,
-             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, kofs, tri};
+             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tune_group(), tune_chunk(), kofs, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
   if (passes == 3 && m > BM && pair_enabled()) {
