@@ -433,7 +433,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=12)
     ap.add_argument("--streams", type=int, default=4, help="CUDA streams the layers are issued on")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="time only the dominant 3xTF32 GEMM at n^3 (small profiling case)")
