@@ -59,6 +59,27 @@ struct BlockArgs {
   int vec;  // W and Hinv rows of this block are 16-byte aligned
 };
 
+// Packed pairs of fp32 (low = first) and the sm_100 two-wide fp32 operations;
+// each half is rounded to nearest exactly as the scalar __fmul_rn / __fsub_rn.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // Compact Hinv block: row j keeps columns [32*(j/32), 128) only (the serial
 // part reads its group's diagonal block, the apply part the columns after it).
 constexpr int HS_FLOATS = GROUP * (MAXB + (MAXB - GROUP) + (MAXB - 2 * GROUP) + (MAXB - 3 * GROUP));
@@ -299,19 +320,17 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
 #pragma unroll 1
     for (int c2 = cb + GROUP; c2 < cend; c2 += 4) {
       float* wc = wsm + (c2 - GROUP) * ROWS + t;
-      float v0 = wc[0], v1 = wc[ROWS], v2 = wc[2 * ROWS], v3 = wc[3 * ROWS];
+      // two columns per packed f32x2 operation (each half rounded as the scalar op)
+      uint64_t v01 = pack2(wc[0], wc[ROWS]), v23 = pack2(wc[2 * ROWS], wc[3 * ROWS]);
 #pragma unroll
       for (int j = 0; j < GROUP; ++j) {
-        const float4 h = *reinterpret_cast<const float4*>(hg + j * hstride + (c2 - cb));
-        v0 = __fsub_rn(v0, __fmul_rn(ev[j], h.x));
-        v1 = __fsub_rn(v1, __fmul_rn(ev[j], h.y));
-        v2 = __fsub_rn(v2, __fmul_rn(ev[j], h.z));
-        v3 = __fsub_rn(v3, __fmul_rn(ev[j], h.w));
+        const ulonglong2 h = *reinterpret_cast<const ulonglong2*>(hg + j * hstride + (c2 - cb));
+        const uint64_t e2 = pack2(ev[j], ev[j]);
+        v01 = sub_f32x2(v01, mul_f32x2(e2, h.x));
+        v23 = sub_f32x2(v23, mul_f32x2(e2, h.y));
       }
-      wc[0] = v0;
-      wc[ROWS] = v1;
-      wc[2 * ROWS] = v2;
-      wc[3 * ROWS] = v3;
+      unpack2(v01, wc[0], wc[ROWS]);
+      unpack2(v23, wc[2 * ROWS], wc[3 * ROWS]);
     }
   }
   if (want_stats && rv) {
