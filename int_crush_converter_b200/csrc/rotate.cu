@@ -26,6 +26,67 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const T* __restrict__ 
   store_row_smem(s, len, out + row * ldo + c0);
 }
 
+// Register-only row rotation for 16 <= rot <= 512: every warp streams groups
+// global -> registers -> butterflies -> global with no shared memory and no
+// barrier, 32/L groups per warp pass (L = rot/16 lanes per group, 16
+// consecutive elements per lane).  Rows are `nb` batches of `rows` rows of
+// which the first `valid` exist in the source (the rest are zero padding);
+// columns >= N are zero padding.  Same operations as hadamard_smem.
+template <typename T>
+__global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ src, int64_t N, int64_t ld,
+                                                          int64_t bstride, int64_t rows, int64_t valid, int64_t nb,
+                                                          int rot, float* __restrict__ out, int64_t ldo,
+                                                          int64_t ostride, int64_t npad) {
+  const int L = rot / 16, gpw = 32 / L;
+  const int lane = threadIdx.x & 31, l = lane & (L - 1);
+  const int64_t ngr = npad / rot;                    // groups per row
+  const int64_t tasks = cdiv(nb * rows * ngr, (int64_t)gpw);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  constexpr int V = 16 / sizeof(T);
+  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < tasks; task += warps) {
+    const int64_t g = task * gpw + lane / L;          // global group index
+    const bool act = g < nb * rows * ngr;
+    const int64_t rg = act ? g / ngr : 0;             // batch-row
+    const int64_t col = (act ? g - rg * ngr : 0) * rot + 16 * l;
+    const int64_t b = rg / rows, r = rg - b * rows;
+    float v[16];
+    const T* p = src + b * bstride + r * ld + col;
+    if (act && r < valid && col + 16 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int q = 0; q < 16 / V; ++q) {
+        const uint4 raw = reinterpret_cast<const uint4*>(p)[q];
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int u = 0; u < V; ++u) v[q * V + u] = load_as_f32(e + u);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = (act && r < valid && col + j < N) ? load_as_f32(p + j) : 0.f;
+    }
+    hadamard_regs16(v, rot, l);
+    if (act) {
+      float* o = out + b * ostride + r * ldo + col;
+      if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<float4*>(o)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = v[j];
+      }
+    }
+  }
+}
+
+template <typename T>
+void launch_rotate_regs(const T* src, int64_t N, int64_t ld, int64_t bstride, int64_t rows, int64_t valid,
+                        int64_t nb, int rot, float* out, int64_t ldo, int64_t ostride, int64_t npad,
+                        cudaStream_t st) {
+  const int64_t tasks = cdiv(nb * rows * (npad / rot), (int64_t)(32 / (rot / 16)));
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(tasks, 8), 148 * 16);
+  rotate_regs_kernel<T><<<grid, 256, 0, st>>>(src, N, ld, bstride, rows, valid, nb, rot, out, ldo, ostride, npad);
+}
+
 // Row pass of R^T H R: every row of H gets the group Hadamard along its
 // columns (H R).  Rows >= n and columns >= n are the zero padding.
 __global__ void __launch_bounds__(256) hess_rows_kernel(const float* __restrict__ H, int64_t n, int64_t ldh,
@@ -151,6 +212,18 @@ int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, 
   if (ldo < npad) return fail(IC_ERR_INVALID, "rotate_weights: ldo < padded width");
   if (M == 0 || npad == 0) return IC_OK;
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_weights: too many rows");
+  if (hadamard_regs_ok(r)) {
+    switch (dtype) {
+      case IC_F32: launch_rotate_regs((const float*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st); break;
+      case IC_F16: launch_rotate_regs((const __half*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st); break;
+      case IC_BF16:
+        launch_rotate_regs((const __nv_bfloat16*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st);
+        break;
+      default: return fail(IC_ERR_INVALID, "rotate_weights: unknown dtype %d", dtype);
+    }
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
   dim3 grid((unsigned)M, (unsigned)cdiv(npad, ROT_CHUNK));
   switch (dtype) {
     case IC_F32: rotate_rows_kernel<float><<<grid, 256, 0, st>>>((const float*)W, N, ldw, r, out, ldo, npad); break;
@@ -175,8 +248,12 @@ int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int r
     return fail(IC_ERR_INVALID, "Block size %lld is not divisible by rot_size %d", (long long)n, rot);
   if (npad > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_hessian: too large");
   const int64_t ostride = npad * ldo;
-  dim3 g1((unsigned)npad, (unsigned)cdiv(npad, ROT_CHUNK), (unsigned)nbatch);
-  hess_rows_kernel<<<g1, 256, 0, st>>>(H, n, ldh, n * ldh, r, out_hi, npad, ldo, ostride);
+  if (hadamard_regs_ok(r)) {
+    launch_rotate_regs(H, n, ldh, n * ldh, npad, n, nbatch, r, out_hi, ldo, ostride, npad, st);
+  } else {
+    dim3 g1((unsigned)npad, (unsigned)cdiv(npad, ROT_CHUNK), (unsigned)nbatch);
+    hess_rows_kernel<<<g1, 256, 0, st>>>(H, n, ldh, n * ldh, r, out_hi, npad, ldo, ostride);
+  }
   IC_CHECK_LAUNCH();
   if (r == 256) {
     dim3 g2((unsigned)cdiv(npad, COLS_R), (unsigned)(npad / 256), (unsigned)nbatch);
