@@ -721,7 +721,10 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   // With stats the call stays asynchronous: the inverse's not-positive-definite bit lands in
   // stats[2].  Without stats it synchronises once to return IC_ERR_NOT_PD.
   IC_CUDA(cudaMemsetAsync(w.status, 0, sizeof(unsigned), st));
-  IC_TRY(spd_inverse(w.Hh, w.Hl, npad, ldw, damping, w.inv, w.inv_bytes, st, w.status));
+  // The column loop reads Hinv's lower 128-tiles and its diagonal blocks; when
+  // the block size divides 128 no block straddles a tile, so the upper tiles
+  // are never read and the mirror pass is skipped.
+  IC_TRY(spd_inverse(w.Hh, w.Hl, npad, ldw, damping, w.inv, w.inv_bytes, st, w.status, 128 % block_size != 0));
   LoopArgs L{};
   L.W = w.Wk; L.ldw = ldw; L.W0 = w.W0; L.ldw0 = ldw; L.M = M; L.N = npad; L.h_hi = w.Hh; L.h_lo = w.Hl;
   L.ldh = ldw; L.B = block_size; L.SB = (LAYER_SB / block_size) * block_size;

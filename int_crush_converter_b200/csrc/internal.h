@@ -18,8 +18,9 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
 int gemm_prepare();
 int transpose(const float* in_hi, const float* in_lo, int64_t rows, int64_t cols, int64_t ldi,
               float alpha, float* out_hi, float* out_lo, int64_t ldo, cudaStream_t st);
+// full = false: only the lower 128-tiles of H^-1 (diagonal tiles complete) are written
 int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping, void* ws,
-                size_t ws_bytes, cudaStream_t st, unsigned* status = nullptr);
+                size_t ws_bytes, cudaStream_t st, unsigned* status = nullptr, bool full = true);
 size_t spd_inverse_ws(int64_t n);
 int read_and_clear_flags(unsigned* out, cudaStream_t st);
 void register_device_flags(int dev, unsigned* p);

@@ -392,7 +392,7 @@ int transpose(const float* in_hi, const float* in_lo, int64_t rows, int64_t cols
 namespace {
 
 // Everything the inverse enqueues, on c.st.
-int inverse_body(const Ctx& c, int64_t n, float damping) {
+int inverse_body(const Ctx& c, int64_t n, float damping, bool full) {
   if (damping >= 0.f) {
     damp_kernel<<<1, 1024, 0, c.st>>>(c.H.hi, c.H.lo, n, c.ld, damping);
     IC_CHECK_LAUNCH();
@@ -403,6 +403,7 @@ int inverse_body(const Ctx& c, int64_t n, float damping) {
   IC_TRY(invt_rec(c, 0, n));
   // H^-1 = U U^T: lower tiles only, K from the tile row (U is upper triangular), then mirror
   IC_TRY(gemm3(c, n, n, n, 1.f, c.U, c.ld, c.U, c.ld, 0.f, c.H, c.ld, false, 3));
+  if (!full) return IC_OK;  // lower 128-tiles (diagonal tiles complete) suffice for the GPTQ loop
   dim3 grid((unsigned)cdiv(n, 32), (unsigned)cdiv(n, 32));
   mirror_kernel<<<grid, dim3(32, 8), 0, c.st>>>(c.H.hi, c.H.lo, n, c.ld);
   IC_CHECK_LAUNCH();
@@ -421,11 +422,12 @@ struct InvGraph {
   const void *hh, *hl, *ws, *status;
   size_t ws_bytes;
   float damping;
+  bool full;
   cudaGraphExec_t exec;
   unsigned long long kernels, used;
   bool same(const InvGraph& o) const {
     return dev == o.dev && n == o.n && ld == o.ld && hh == o.hh && hl == o.hl && ws == o.ws &&
-           status == o.status && ws_bytes == o.ws_bytes && damping == o.damping;
+           status == o.status && ws_bytes == o.ws_bytes && damping == o.damping && full == o.full;
   }
 };
 constexpr size_t MAX_GRAPHS = 32;
@@ -442,11 +444,11 @@ bool graphs_enabled() {
   return on;
 }
 
-int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_bytes) {
+int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_bytes, bool full) {
   InvGraph key{};
   IC_CUDA(cudaGetDevice(&key.dev));
   key.n = n; key.ld = c.ld; key.hh = c.H.hi; key.hl = c.H.lo; key.ws = ws; key.status = c.flags;
-  key.ws_bytes = ws_bytes; key.damping = damping;
+  key.ws_bytes = ws_bytes; key.damping = damping; key.full = full;
   std::lock_guard<std::mutex> lock(g_graph_mu);
   for (auto& g : g_graphs) {
     if (g.same(key)) {
@@ -465,7 +467,7 @@ int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_by
   cc.st = g_capture[key.dev];
   const unsigned long long k0 = launches();
   IC_CUDA(cudaStreamBeginCapture(cc.st, cudaStreamCaptureModeThreadLocal));
-  const int r = inverse_body(cc, n, damping);
+  const int r = inverse_body(cc, n, damping, full);
   cudaGraph_t graph = nullptr;
   const cudaError_t e = cudaStreamEndCapture(cc.st, &graph);
   if (r != IC_OK) {
@@ -497,7 +499,7 @@ int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_by
 }  // namespace
 
 int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping, void* ws, size_t ws_bytes,
-                cudaStream_t st, unsigned* status) {
+                cudaStream_t st, unsigned* status, bool full) {
   if (n <= 0) return IC_OK;
   if (!h_hi || !h_lo) return fail(IC_ERR_INVALID, "spd_inverse: hi/lo pair required");
   if (ldh % 4) return fail(IC_ERR_INVALID, "spd_inverse: ld must be a multiple of 4");
@@ -516,12 +518,12 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   if (status) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     IC_CUDA(cudaStreamIsCapturing(st, &cs));
-    if (graphs_enabled() && cs == cudaStreamCaptureStatusNone) return inverse_graph(c, n, damping, ws, ws_bytes);
-    return inverse_body(c, n, damping);
+    if (graphs_enabled() && cs == cudaStreamCaptureStatusNone) return inverse_graph(c, n, damping, ws, ws_bytes, full);
+    return inverse_body(c, n, damping, full);
   }
   unsigned prev = 0;
   IC_TRY(read_and_clear_flags(&prev, st));
-  IC_TRY(inverse_body(c, n, damping));
+  IC_TRY(inverse_body(c, n, damping, full));
   unsigned f = 0;
   IC_TRY(read_and_clear_flags(&f, st));
   if (f & DEV_TIMEOUT) return fail(IC_ERR_TIMEOUT, "spd_inverse: a tensor-core wait timed out");

@@ -464,3 +464,21 @@ def test_sharded_layers_world1_match_serial():
         ref = B.quantize_gptq_layer(W, H, rot_size=256)
         assert torch.equal(ref["packed"], got[k]["packed"])
         assert torch.equal(ref["scales"], got[k]["scales"])
+
+
+@pytest.mark.parametrize("bs", [64, 96])
+def test_gptq_layer_block_sizes_vs_oracle(bs):
+    """The fused layer at block sizes that divide 128 (Hinv's upper tiles are not
+    written) and that do not (they are mirrored): proxy within 1% of the oracle."""
+    M, N = 256, 1024
+    W = gi.weight_outlier_cols(80 + bs, M, N)
+    H = gi.hessian_lognormal(90 + bs, N, 2 * N)
+    Wr = R.rotate_weights(W, 256)
+    Hr = R.rotate_hessian(H, 256)
+    ref = R.gptq_quantize_layer(Wr, Hr, bs, 0.01, 4)
+    out = B.quantize_gptq_layer(cu(W).half(), cu(H), rot_size=256, block_size=bs, want_codes=True)
+    q = np_(out["codes"])
+    assert np.array_equal(np_(out["scales"]), ref["scales"])
+    p = R.proxy_loss(Wr, q, ref["scales"].astype(np.float32), ref["zero_points"], Hr)
+    pr = R.proxy_loss(Wr, ref["quantized_W"], ref["scales"].astype(np.float32), ref["zero_points"], Hr)
+    assert abs(p / pr - 1) < 0.01, p / pr
