@@ -482,3 +482,36 @@ def test_gptq_layer_block_sizes_vs_oracle(bs):
     p = R.proxy_loss(Wr, q, ref["scales"].astype(np.float32), ref["zero_points"], Hr)
     pr = R.proxy_loss(Wr, ref["quantized_W"], ref["scales"].astype(np.float32), ref["zero_points"], Hr)
     assert abs(p / pr - 1) < 0.01, p / pr
+
+
+@pytest.mark.parametrize("bits,asym,N,dtype,h_rot", [
+    (8, False, 1024, "half", False),     # INT8 codes, no packing
+    (4, True, 1024, "half", False),      # asymmetric INT4
+    (4, False, 1000, "half", False),     # ragged width: zero padding to 1024
+    (4, False, 768, "bfloat16", False),  # bf16 weights
+    (4, False, 512, "half", True),       # Hessian passed already rotated
+])
+def test_gptq_layer_variants_vs_oracle(bits, asym, N, dtype, h_rot):
+    """Fused layer call across the pipeline's variants: scales and zero-points
+    equal to the oracle's, packed bytes equal to the codes, proxy within 1%."""
+    M = 192
+    W = gi.weight_outlier_cols(300 + N + bits, M, N)
+    H = gi.hessian_lognormal(400 + N + bits, N, 2 * N)
+    Wt = torch.from_numpy(W).to(getattr(torch, dtype))
+    Wq = Wt.float().numpy()  # the values the device sees
+    Wr = R.rotate_weights(Wq, 256)
+    Hr = R.rotate_hessian(H, 256)
+    ref = R.gptq_quantize_layer(Wr, Hr, 128, 0.01, bits, asymmetric=asym)
+    out = B.quantize_gptq_layer(Wt.cuda(), cu(Hr if h_rot else H), rot_size=256, int_bits=bits,
+                                asymmetric=asym, h_rotated=h_rot, want_codes=True)
+    q = np_(out["codes"])
+    npad = Wr.shape[1]
+    assert q.shape == (M, npad)
+    assert np.array_equal(np_(out["scales"]), ref["scales"])
+    if ref["zero_points"] is not None and out["zero_points"] is not None:
+        assert np.array_equal(np_(out["zero_points"]).reshape(-1), np.asarray(ref["zero_points"]).reshape(-1))
+    if bits == 4:
+        assert np.array_equal(np_(B.unpack_int4(out["packed"], npad)), q)
+    p = R.proxy_loss(Wr, q, ref["scales"].astype(np.float32), ref["zero_points"], Hr)
+    pr = R.proxy_loss(Wr, ref["quantized_W"], ref["scales"].astype(np.float32), ref["zero_points"], Hr)
+    assert abs(p / pr - 1) < 0.01, p / pr
