@@ -344,6 +344,10 @@ class LayerStreams:
             dev = torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         self.streams = [torch.cuda.Stream(dev) for _ in range(max(1, n_streams))]
+        # host inputs are copied on a lane's own copy stream, ahead of the lane's
+        # compute by at most two layers (prefetch over PCIe while it computes)
+        self.copy_streams = [torch.cuda.Stream(dev) for _ in self.streams]
+        self._done: list[list[torch.cuda.Event]] = [[] for _ in self.streams]
         self.ws = [LayerWorkspace() for _ in self.streams]
         self.load = [0.0] * len(self.streams)
         self._stats: list[torch.Tensor] = []
@@ -361,14 +365,15 @@ class LayerStreams:
     def fork(self) -> None:
         """Order the streams after the work already queued on the current stream."""
         cur = torch.cuda.current_stream(self.device)
-        for s in self.streams:
+        for s in self.streams + self.copy_streams:
             s.wait_stream(cur)
         self.load = [0.0] * len(self.streams)
+        self._done = [[] for _ in self.streams]
 
     def join(self) -> None:
         """Order the current stream after everything submitted (no host wait)."""
         cur = torch.cuda.current_stream(self.device)
-        for s in self.streams:
+        for s in self.streams + self.copy_streams:
             cur.wait_stream(s)
 
     def submit(self, W: torch.Tensor, H: torch.Tensor, then=None, **kw) -> dict:
@@ -381,18 +386,26 @@ class LayerStreams:
         i = min(range(len(self.load)), key=self.load.__getitem__)
         self.load[i] += float(M) * N * N + float(N) ** 3
         s = self.streams[i]
+        if not (W.is_cuda and H.is_cuda):
+            cs = self.copy_streams[i]
+            done = self._done[i]
+            if len(done) >= 2:
+                cs.wait_event(done[-2])  # at most two layers of inputs ahead of the lane
+            with torch.cuda.stream(cs):
+                if not W.is_cuda:
+                    W = W.to(self.device, non_blocking=True)
+                if not H.is_cuda:
+                    H = H.to(self.device, non_blocking=True)
+            s.wait_stream(cs)
+        for t in (W, H):
+            t.record_stream(s)
         with torch.cuda.stream(s):
-            if not W.is_cuda:
-                W = W.to(self.device, non_blocking=True)
-            else:
-                W.record_stream(s)
-            if not H.is_cuda:
-                H = H.to(self.device, non_blocking=True)
-            else:
-                H.record_stream(s)
             res = quantize_gptq_layer(W, H, ws=self.ws[i], check=False, **kw)
             if then is not None:
                 then(res)
+            ev = torch.cuda.Event()
+            ev.record(s)
+        self._done[i] = self._done[i][-1:] + [ev]
         self._stats.append(res["stats"])
         return res
 
