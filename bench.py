@@ -426,6 +426,74 @@ def run_hbm_kernels(reps: int = 5) -> None:
         print(json.dumps(o), flush=True)
 
 
+def run_configs() -> None:
+    """The BASELINE configs other than the headline one, each through the public
+    API on device-resident synthetic inputs of the config's shapes (seeded),
+    timed with CUDA events after a warm-up; one JSON line per config."""
+    import int_crush_converter_b200 as B
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(21)
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    def weights(m, n, std, outlier_frac=0.0, outlier_mult=1.0):
+        W = torch.randn(m, n, generator=g, device=dev) * std
+        if outlier_frac:
+            k = max(1, int(n * outlier_frac))
+            cols = torch.randperm(n, generator=g, device=dev)[:k]
+            W[:, cols] *= outlier_mult
+        return W.half()
+
+    lines = []
+    # config 1: RTN INT4 sym rot256, 8 x [4096,4096]
+    W1 = [weights(4096, 4096, 0.02, 0.001, 20.0) for _ in range(8)]
+    ms = timed(lambda: [B.rtn_quantize_fused(W, 256, int_bits=4, want_codes=False) for W in W1], 3)
+    lines.append(dict(config=1, workload="RTN INT4 sym rot256, 8 fp16 layers [4096,4096]", params=8 * 4096 * 4096, ms=ms))
+    del W1
+    # config 2: RTN INT8 sym rot64 with the clipping-ratio search, 16 x [3072,3072] + 16 x [12288,3072]
+    t = torch.distributions.StudentT(torch.tensor(3.0, device=dev))
+
+    def w2(m, n):
+        W = torch.randn(m, n, generator=g, device=dev) * 0.02
+        mask = torch.rand(m, n, generator=g, device=dev) < 0.01
+        W = W + mask * (0.02 * t.sample((m, n)))
+        return W.half()
+    W2 = [w2(3072, 3072) for _ in range(16)] + [w2(12288, 3072) for _ in range(16)]
+    ratios = [0.8, 0.85, 0.9, 0.95, 1.0]
+    ms = timed(lambda: [B.rtn_quantize_fused(W, 64, int_bits=8, clipping_ratios=ratios, want_codes=True,
+                                             want_packed=False) for W in W2], 2)
+    lines.append(dict(config=2, workload="RTN INT8 sym rot64, clipping ratios {0.8..1.0}, 16 x [3072,3072] + "
+                      "16 x [12288,3072] fp16 (N(0,0.02^2) + Student-t(3) tails on 1%)",
+                      params=16 * 3072 * 3072 + 16 * 12288 * 3072, ms=ms))
+    del W2
+    # config 4: LDLQ INT4 rot256, 2 iterations, 8 greedy passes, weight-only Hessian; one [8192,8192] layer
+    W4 = weights(8192, 8192, 0.015, 0.0005, 30.0)
+
+    def ldlq():
+        Wr = B.rotate_weights(W4, 256)
+        return B.ldlq_quantize_layer(Wr, None, block_size=128, int_bits=4, iterations=2, greedy_passes=8)
+    import warnings
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        ms = timed(ldlq, 1)
+    lines.append(dict(config=4, workload="LDLQ INT4 rot256, 2 iterations, 8 greedy passes, weight-only Hessian, "
+                      "one fp16 layer [8192,8192] (N(0,0.015^2), 0.05% columns x30)", params=8192 * 8192, ms=ms))
+    for d in lines:
+        d.update(metric="Mparams quantized/s", value=round(d["params"] / (d["ms"] * 1e-3) / 1e6, 2),
+                 ms=round(d["ms"], 3), data="synthetic, device-resident")
+        print(json.dumps(d), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,7 +509,11 @@ def main() -> None:
                     help="time the HBM-bound kernels (RTN, rotations) alone and exit")
     ap.add_argument("--one-step", action="store_true",
                     help="quantize one set once and exit (for an ncu launch list of exactly one step)")
+    ap.add_argument("--configs", action="store_true", help="time BASELINE configs 1, 2 and 4 and exit")
     args = ap.parse_args()
+    if args.configs:
+        run_configs()
+        return
     if args.one_step:
         import int_crush_converter_b200 as B
         dev = torch.device("cuda", 0)
