@@ -12,7 +12,7 @@ summation order as torch's CPU kernels; the golden fixtures in
 ``tests/golden`` pin how close that is.
 
 Third-party arithmetic the reference delegates to torch (not under the
-reference tree; torch 2.11.0 in the survey container, ``pyproject.toml`` pins
+reference tree; torch 2.11.0 where the fixtures were generated, ``pyproject.toml`` pins
 only ``torch>=2.1``):
   * ``torch.linalg.cholesky`` + ``torch.cholesky_inverse`` = LAPACK
     ``spotrf`` + ``spotri``: restated with ``scipy.linalg.lapack`` (same
