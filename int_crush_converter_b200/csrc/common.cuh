@@ -5,6 +5,7 @@
 // non-positive pivot, an out-of-range code) are recorded in a per-device
 // status word that the host reads back; kernels never trap.
 #pragma once
+#include <atomic>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -29,6 +30,21 @@ int fail(int code, const char* fmt, ...);
       return ::ic::fail(IC_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,           \
                         cudaGetErrorString(_e), __FILE__, __LINE__);           \
   } while (0)
+
+// Run `fn` (returning an IC_* status) once per device: kernel attributes such
+// as the dynamic shared-memory opt-in are per device, so a process driving
+// several GPUs must set them on each.
+template <typename F>
+inline int once_per_device(std::atomic<unsigned long long>& done, F&& fn) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(IC_ERR_CUDA, "cudaGetDevice failed");
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load() & bit) return IC_OK;
+  const int r = fn();
+  if (r != IC_OK) return r;
+  done.fetch_or(bit);
+  return IC_OK;
+}
 
 void count_launch();
 void add_launches(unsigned long long n);  // kernels a replayed CUDA graph runs

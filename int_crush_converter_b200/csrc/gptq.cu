@@ -524,12 +524,12 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
     hb_hi = cv.take<float>((size_t)L.N * ldb2);
     hb_lo = cv.take<float>((size_t)L.N * ldb2);
   }
-  static bool attr = false;
-  if (!attr) {
-    IC_CUDA(cudaFuncSetAttribute(block_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BLOCK_SMEM));
-    IC_CUDA(cudaFuncSetAttribute(block_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BLOCK_SMEM));
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  IC_TRY(once_per_device(attr, [&]() -> int {
+      IC_CUDA(cudaFuncSetAttribute(block_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BLOCK_SMEM));
+      IC_CUDA(cudaFuncSetAttribute(block_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BLOCK_SMEM));
+      return IC_OK;
+    }));
   if (L.row_sqerr) fill_kernel_d<<<grid1(L.M), 256, 0, st>>>(L.row_sqerr, L.M, 0.0);
   if (L.row_maxerr) fill_kernel_f<<<grid1(L.M), 256, 0, st>>>(L.row_maxerr, L.M, 0.f);
   IC_CHECK_LAUNCH();

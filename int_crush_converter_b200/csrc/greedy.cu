@@ -151,11 +151,11 @@ extern "C" int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq
   float* eh = cv.take<float>((size_t)M * lde);
   float* el = cv.take<float>((size_t)M * lde);
   float* cross = cv.take<float>((size_t)M * GB);
-  static bool attr = false;
-  if (!attr) {
-    IC_CUDA(cudaFuncSetAttribute(greedy_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GSMEM));
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  IC_TRY(once_per_device(attr, [&]() -> int {
+      IC_CUDA(cudaFuncSetAttribute(greedy_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GSMEM));
+      return IC_OK;
+    }));
   {
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(M * N, 256), 148 * 16));
     err_init_kernel<<<blocks, 256, 0, st>>>(W, ldw, Q, ldq, scale2d, lds, M, N, eh, el, lde);

@@ -139,11 +139,11 @@ extern "C" int ic_piso(const float* W, int64_t M, int64_t N, int64_t ldw, const 
   h.divisor = divisor; h.nc = ncoarse; h.nf = nfine; h.scales = scales; h.zp = zp;
   for (int i = 0; i < ncoarse; ++i) h.coarse[i] = coarse[i];
   for (int i = 0; i < nfine; ++i) h.fine[i] = fine[i];
-  static bool attr = false;
-  if (!attr) {
-    IC_CUDA(cudaFuncSetAttribute(piso_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(MAXN * 8)));
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  IC_TRY(once_per_device(attr, [&]() -> int {
+      IC_CUDA(cudaFuncSetAttribute(piso_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(MAXN * 8)));
+      return IC_OK;
+    }));
   piso_kernel<<<(unsigned)M, NT, (size_t)N * 8, (cudaStream_t)stream>>>(h);
   IC_CHECK_LAUNCH();
   return IC_OK;

@@ -480,11 +480,11 @@ int launch_rtn(RtnArgs& a, int64_t M, cudaStream_t st) {
   if (a.npad > MAX_ROW)
     return fail(IC_ERR_UNSUPPORTED, "rtn: row of %lld elements exceeds %lld", (long long)a.npad, (long long)MAX_ROW);
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rtn: too many rows");
-  static bool attr = false;
-  if (!attr) {
-    IC_CUDA(cudaFuncSetAttribute(rtn_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(MAX_ROW * 4)));
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  IC_TRY(once_per_device(attr, [&]() -> int {
+      IC_CUDA(cudaFuncSetAttribute(rtn_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(MAX_ROW * 4)));
+      return IC_OK;
+    }));
   rtn_row_kernel<<<(unsigned)M, NT, (size_t)a.npad * 4, st>>>(a);
   IC_CHECK_LAUNCH();
   return IC_OK;
