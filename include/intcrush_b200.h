@@ -84,7 +84,8 @@ int ic_rtn_codes(const float* W, int64_t M, int64_t N, int64_t ldw, int bits, in
                  int64_t group_size, const uint16_t* scales_f16, const int8_t* zp,
                  int8_t* codes, int64_t ldc, void* stream);
 
-/* Fused single pass over each row: load W (fp16/bf16/fp32), rotate (rot as in
+/* Fused single pass over each row: load W (fp16/bf16/fp32), zero |w| > 1000
+ * (the pipeline's outlier sanitize, pipeline.py:527-537), rotate (rot as in
  * ic_rotate_weights), per-row scale search, round-half-away, clamp, write int8
  * codes [M, npad] and/or packed INT4 [M, ceil(npad/2)], fp16 scales [M], int8
  * zp [M], and the verify statistics of pipeline.py:919-931 per row (sum of
@@ -188,8 +189,9 @@ int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw
                         int64_t ldp, double* row_sqerr, float* row_maxerr, int gemm_passes,
                         void* stream);
 
-/* One whole GPTQ layer as pipeline.py:547-559 + 702-809 + 919-931 + 1010-1013
- * run it: rotate W (fp16/bf16/fp32) and H, row params, damping, inverse,
+/* One whole GPTQ layer as pipeline.py:527-559 + 702-809 + 919-931 + 1010-1013
+ * run it: zero |w| > 1000 (outlier sanitize), rotate W (fp16/bf16/fp32) and
+ * H, row params, damping, inverse,
  * column loop, pack, verify statistics.  H fp32 [N_in, N_in] (already in the
  * rotated space when h_rotated != 0).  Outputs: packed uint8 [M, npad/2]
  * (bits 4) and/or codes int8 [M, npad]; scales_f16 [M]; zp int8 [M] (bits 4

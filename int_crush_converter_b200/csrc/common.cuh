@@ -46,6 +46,10 @@ inline int once_per_device(std::atomic<unsigned long long>& done, F&& fn) {
   return IC_OK;
 }
 
+// |w| above this is corrupted data and zeroed before rotation in the fused
+// per-layer calls (config.WEIGHT_OUTLIER_CLAMP, applied at pipeline.py:527-537)
+constexpr float WEIGHT_OUTLIER_CLAMP = 1000.f;
+
 void count_launch();
 void add_launches(unsigned long long n);  // kernels a replayed CUDA graph runs
 unsigned long long launches();

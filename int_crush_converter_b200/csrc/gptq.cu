@@ -706,7 +706,7 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   if (workspace_bytes < need)
     return fail(IC_ERR_WORKSPACE, "gptq_layer: workspace too small (%zu < %zu)", workspace_bytes, need);
   if (h_rotated && N_in != npad) return fail(IC_ERR_INVALID, "pre-rotated Hessian needs in_features % rot_size == 0");
-  IC_TRY(rotate_weights(W, dtype, M, N_in, ldw_in, rot, w.W0, ldw, st));
+  IC_TRY(rotate_weights(W, dtype, M, N_in, ldw_in, rot, w.W0, ldw, st, WEIGHT_OUTLIER_CLAMP));
   IC_CUDA(cudaMemcpyAsync(w.Wk, w.W0, (size_t)M * ldw * 4, cudaMemcpyDeviceToDevice, st));
   if (h_rotated || r <= 1) {
     IC_TRY(split_tf32(H, npad, npad, ldh_in, w.Hh, w.Hl, ldw, st));

@@ -4,8 +4,10 @@
 #include <stdint.h>
 
 namespace ic {
+// clamp > 0: weights with |w| > clamp are zeroed on load (the pipeline's
+// outlier sanitize, pipeline.py:527-537); NaN passes through
 int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot, float* out,
-                   int64_t ldo, cudaStream_t st);
+                   int64_t ldo, cudaStream_t st, float clamp = 0.f);
 int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int rot, float* out_hi,
                    float* out_lo, int64_t npad, int64_t ldo, cudaStream_t st);
 int split_tf32(const float* in, int64_t rows, int64_t cols, int64_t ldi, float* hi, float* lo,

@@ -15,12 +15,14 @@ constexpr int ROT_CHUNK = 8192;  // columns per CTA for the row rotation
 template <typename T>
 __global__ void __launch_bounds__(256) rotate_rows_kernel(const T* __restrict__ W, int64_t N, int64_t ldw,
                                                           int rot, float* __restrict__ out, int64_t ldo,
-                                                          int64_t npad) {
+                                                          int64_t npad, float clamp) {
   __shared__ __align__(16) float s[ROT_CHUNK];
   const int64_t row = blockIdx.x;
   const int64_t c0 = (int64_t)blockIdx.y * ROT_CHUNK;
   const int len = (int)((npad - c0) < ROT_CHUNK ? (npad - c0) : ROT_CHUNK);
   load_row_smem(W + row * ldw, c0, N, len, s);
+  if (clamp > 0.f)
+    for (int i = threadIdx.x; i < len; i += blockDim.x) s[i] = fabsf(s[i]) > clamp ? 0.f : s[i];
   __syncthreads();
   hadamard_row(s, len, rot);
   store_row_smem(s, len, out + row * ldo + c0);
@@ -36,7 +38,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ src, int64_t N, int64_t ld,
                                                           int64_t bstride, int64_t rows, int64_t valid, int64_t nb,
                                                           int rot, float* __restrict__ out, int64_t ldo,
-                                                          int64_t ostride, int64_t npad) {
+                                                          int64_t ostride, int64_t npad, float clamp) {
   const int L = rot / 16, gpw = 32 / L;
   const int lane = threadIdx.x & 31, l = lane & (L - 1);
   const int64_t ngr = npad / rot;                    // groups per row
@@ -63,6 +65,10 @@ __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ 
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = (act && r < valid && col + j < N) ? load_as_f32(p + j) : 0.f;
     }
+    if (clamp > 0.f) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = fabsf(v[j]) > clamp ? 0.f : v[j];
+    }
     hadamard_regs16(v, rot, l);
     if (act) {
       float* o = out + b * ostride + r * ldo + col;
@@ -81,10 +87,11 @@ __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ 
 template <typename T>
 void launch_rotate_regs(const T* src, int64_t N, int64_t ld, int64_t bstride, int64_t rows, int64_t valid,
                         int64_t nb, int rot, float* out, int64_t ldo, int64_t ostride, int64_t npad,
-                        cudaStream_t st) {
+                        cudaStream_t st, float clamp = 0.f) {
   const int64_t tasks = cdiv(nb * rows * (npad / rot), (int64_t)(32 / (rot / 16)));
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(tasks, 8), 148 * 16);
-  rotate_regs_kernel<T><<<grid, 256, 0, st>>>(src, N, ld, bstride, rows, valid, nb, rot, out, ldo, ostride, npad);
+  rotate_regs_kernel<T><<<grid, 256, 0, st>>>(src, N, ld, bstride, rows, valid, nb, rot, out, ldo, ostride, npad,
+                                               clamp);
 }
 
 // Row pass of R^T H R: every row of H gets the group Hadamard along its
@@ -204,7 +211,7 @@ bool rot_ok(int rot) { return rot == 0 || (rot >= 2 && rot <= 1024 && (rot & (ro
 }  // namespace
 
 int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot, float* out,
-                   int64_t ldo, cudaStream_t st) {
+                   int64_t ldo, cudaStream_t st, float clamp) {
   if (!rot_ok(rot)) return fail(IC_ERR_INVALID, "rot_size must be a power of 2, got %d", rot);
   if (M < 0 || N < 0 || ldw < N) return fail(IC_ERR_INVALID, "rotate_weights: bad shape");
   const int r = rot ? rot : 1;
@@ -214,10 +221,10 @@ int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, 
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_weights: too many rows");
   if (hadamard_regs_ok(r)) {
     switch (dtype) {
-      case IC_F32: launch_rotate_regs((const float*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st); break;
-      case IC_F16: launch_rotate_regs((const __half*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st); break;
+      case IC_F32: launch_rotate_regs((const float*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp); break;
+      case IC_F16: launch_rotate_regs((const __half*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp); break;
       case IC_BF16:
-        launch_rotate_regs((const __nv_bfloat16*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st);
+        launch_rotate_regs((const __nv_bfloat16*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp);
         break;
       default: return fail(IC_ERR_INVALID, "rotate_weights: unknown dtype %d", dtype);
     }
@@ -226,10 +233,10 @@ int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, 
   }
   dim3 grid((unsigned)M, (unsigned)cdiv(npad, ROT_CHUNK));
   switch (dtype) {
-    case IC_F32: rotate_rows_kernel<float><<<grid, 256, 0, st>>>((const float*)W, N, ldw, r, out, ldo, npad); break;
-    case IC_F16: rotate_rows_kernel<__half><<<grid, 256, 0, st>>>((const __half*)W, N, ldw, r, out, ldo, npad); break;
+    case IC_F32: rotate_rows_kernel<float><<<grid, 256, 0, st>>>((const float*)W, N, ldw, r, out, ldo, npad, clamp); break;
+    case IC_F16: rotate_rows_kernel<__half><<<grid, 256, 0, st>>>((const __half*)W, N, ldw, r, out, ldo, npad, clamp); break;
     case IC_BF16:
-      rotate_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)W, N, ldw, r, out, ldo, npad);
+      rotate_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)W, N, ldw, r, out, ldo, npad, clamp);
       break;
     default: return fail(IC_ERR_INVALID, "rotate_weights: unknown dtype %d", dtype);
   }

@@ -24,6 +24,7 @@ struct RtnArgs {
   int64_t N, ldw, npad, gs;
   int rot, bits, asym, G, nratios, given, zero_group_zp0;
   float ratios[MAX_RATIOS];
+  float clamp;  // > 0: |w| > clamp zeroed on load (the pipeline's outlier sanitize)
   const uint16_t* in_scales;
   const int8_t* in_zp;
   uint16_t* scales;
@@ -184,6 +185,10 @@ __global__ void __launch_bounds__(NT) rtn_row_kernel(const RtnArgs a) {
   else
     load_row_smem(reinterpret_cast<const float*>(a.W) + row * a.ldw, 0, a.N, (int)a.npad, row_s);
   __syncthreads();
+  if (a.clamp > 0.f) {
+    for (int64_t i = threadIdx.x; i < a.npad; i += NT) row_s[i] = fabsf(row_s[i]) > a.clamp ? 0.f : row_s[i];
+    __syncthreads();
+  }
   if (a.rot > 1) hadamard_row(row_s, (int)a.npad, a.rot);
   double sq = 0.0;
   float mx = 0.f;
@@ -299,6 +304,10 @@ __global__ void __launch_bounds__(NT) rtn_regs_kernel(const RtnArgs a) {
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = (act && c0 + j < a.N) ? load_as_f32(src + j) : 0.f;
+  }
+  if (a.clamp > 0.f) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = fabsf(v[j]) > a.clamp ? 0.f : v[j];
   }
   if (a.rot > 1) hadamard_regs16(v, a.rot, ch & (a.rot / 16 - 1));
 
@@ -548,6 +557,7 @@ extern "C" int ic_rtn_fused(const void* W, int dtype, int64_t M, int64_t N, int6
   a.W = W; a.dtype = dtype; a.N = N; a.ldw = ldw; a.npad = cdiv(N, r) * r; a.gs = a.npad;
   a.rot = rot; a.bits = bits; a.asym = asym; a.G = 1; a.given = 0;
   a.zero_group_zp0 = (bits == 4);
+  a.clamp = WEIGHT_OUTLIER_CLAMP;
   a.scales = scales_f16; a.zp = zp; a.codes = codes; a.ldc = a.npad; a.packed = packed;
   a.ldp = (a.npad + 1) / 2; a.row_sqerr = row_sqerr; a.row_maxerr = row_maxerr;
   IC_TRY(fill_ratios(a, ratios, nratios));

@@ -253,7 +253,8 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
                         h_rotated: bool = False, want_codes: bool = False, want_packed: bool = True,
                         out: dict | None = None, ws: LayerWorkspace | None = None, check: bool = True,
                         update_passes: int = 1) -> dict:
-    """Fused GPTQ layer on the GPU: pipeline.py:547-559 + 702-809 + 919-931 + 1010-1013.
+    """Fused GPTQ layer on the GPU: pipeline.py:527-559 + 702-809 + 919-931 + 1010-1013
+    (outlier sanitize |w| > 1000 -> 0, rotations, GPTQ, packing, verify).
 
     W fp16/bf16/fp32 [out, in] (unrotated), H fp32 [in, in] (unrotated unless
     ``h_rotated``).  Returns a dict of device tensors: ``packed`` uint8

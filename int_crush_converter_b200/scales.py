@@ -135,10 +135,11 @@ def quantize_weights_int8_asymmetric(W, scales, zero_points):
 def rtn_quantize_fused(W: torch.Tensor, rot_size: int, int_bits: int = 4, asymmetric: bool = False,
                        clipping_ratios: list[float] | None = None, want_codes: bool = True,
                        want_packed: bool = True) -> dict:
-    """One pass: rotate + per-row scale search + RTN + pack + verify statistics.
+    """One pass: sanitize + rotate + per-row scale search + RTN + pack + verify statistics.
 
-    The device-resident form of pipeline.py:547-559 + 890-931 + 1010-1013 for
-    one RTN layer.  W fp16/bf16/fp32 [out, in] -> dict with ``codes`` int8
+    The device-resident form of pipeline.py:527-559 + 890-931 + 1010-1013 for
+    one RTN layer (weights with |w| > 1000 are zeroed first, as the pipeline
+    does before rotating).  W fp16/bf16/fp32 [out, in] -> dict with ``codes`` int8
     [out, in_pad] (optional), ``packed`` uint8 [out, ceil(in_pad/2)] (INT4),
     ``scales`` fp16 [out, 1], ``zero_points`` int8 [out, 1] (asymmetric) and
     ``stats`` fp64 [mse, max_err] of the verify step, all on the GPU.

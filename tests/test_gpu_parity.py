@@ -515,3 +515,25 @@ def test_gptq_layer_variants_vs_oracle(bits, asym, N, dtype, h_rot):
     p = R.proxy_loss(Wr, q, ref["scales"].astype(np.float32), ref["zero_points"], Hr)
     pr = R.proxy_loss(Wr, ref["quantized_W"], ref["scales"].astype(np.float32), ref["zero_points"], Hr)
     assert abs(p / pr - 1) < 0.01, p / pr
+
+
+def test_fused_calls_sanitize_outliers_like_the_pipeline():
+    """pipeline.py:527-537 zeroes |w| > 1000 before rotating; the fused layer
+    calls do the same (the plain rotate_weights mirror does not)."""
+    M, N = 128, 512
+    W = gi.weight_outlier_cols(500, M, N)
+    W[3, 7] = 5000.0
+    W[10, 100] = -2000.0
+    W[20, 300] = np.inf
+    Ws = np.where(np.abs(W) > 1000.0, 0.0, W).astype(np.float32)
+    H = gi.hessian_lognormal(501, N, 2 * N)
+    Wr = R.rotate_weights(Ws, 256)
+    Hr = R.rotate_hessian(H, 256)
+    ref = R.gptq_quantize_layer(Wr, Hr, 128, 0.01, 4)
+    out = B.quantize_gptq_layer(cu(W), cu(H), rot_size=256, want_codes=True)
+    assert np.array_equal(np_(out["scales"]), ref["scales"])
+    rt = B.rtn_quantize_fused(cu(W), 256, int_bits=4)
+    s_ref = R.calculate_scales(Wr, Wr.shape[1])
+    assert np.array_equal(np_(rt["scales"]).reshape(-1), np.asarray(s_ref).reshape(-1))
+    assert np.isfinite(np_(B.rotate_weights(cu(Ws), 256))).all()
+    assert not np.isfinite(np_(B.rotate_weights(cu(W), 256))).all()  # the mirror keeps the reference's semantics
