@@ -28,3 +28,4 @@ from .scales import (
 from .types import QuantizationResult
 
 __version__ = "0.1.0"
+from .smoothquant import apply_smoothing_to_weight, _transform_hessian_for_smoothquant  # noqa: E402,F401

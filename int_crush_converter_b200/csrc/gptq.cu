@@ -689,7 +689,7 @@ extern "C" size_t ic_gptq_layer_workspace_size(int64_t M, int64_t N_in, int rot)
 }
 
 extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, int64_t ldw_in, const float* H,
-                             int64_t ldh_in, int h_rotated, int rot, int bits, int asym, int block_size, float damping,
+                             int64_t ldh_in, const float* smoothing, int h_rotated, int rot, int bits, int asym, int block_size, float damping,
                              int update_passes,
                              int8_t* codes, uint8_t* packed, uint16_t* scales_f16, int8_t* zp_out, double* stats,
                              void* workspace, size_t workspace_bytes, void* stream) {
@@ -706,12 +706,12 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   if (workspace_bytes < need)
     return fail(IC_ERR_WORKSPACE, "gptq_layer: workspace too small (%zu < %zu)", workspace_bytes, need);
   if (h_rotated && N_in != npad) return fail(IC_ERR_INVALID, "pre-rotated Hessian needs in_features % rot_size == 0");
-  IC_TRY(rotate_weights(W, dtype, M, N_in, ldw_in, rot, w.W0, ldw, st, WEIGHT_OUTLIER_CLAMP));
+  IC_TRY(rotate_weights(W, dtype, M, N_in, ldw_in, rot, w.W0, ldw, st, WEIGHT_OUTLIER_CLAMP, smoothing));
   IC_CUDA(cudaMemcpyAsync(w.Wk, w.W0, (size_t)M * ldw * 4, cudaMemcpyDeviceToDevice, st));
   if (h_rotated || r <= 1) {
-    IC_TRY(split_tf32(H, npad, npad, ldh_in, w.Hh, w.Hl, ldw, st));
+    IC_TRY(split_tf32(H, npad, npad, ldh_in, w.Hh, w.Hl, ldw, st, smoothing));
   } else {
-    IC_TRY(rotate_hessian(H, 1, N_in, ldh_in, rot, w.Hh, w.Hl, npad, ldw, st));
+    IC_TRY(rotate_hessian(H, 1, N_in, ldh_in, rot, w.Hh, w.Hl, npad, ldw, st, smoothing));
   }
   const bool has_zp = bits == 4 || asym;
   IC_TRY(ic_gptq_row_params(w.W0, M, npad, ldw, bits, asym, w.scale, has_zp ? w.zp : nullptr, st));

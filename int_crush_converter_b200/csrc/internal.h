@@ -7,11 +7,13 @@ namespace ic {
 // clamp > 0: weights with |w| > clamp are zeroed on load (the pipeline's
 // outlier sanitize, pipeline.py:527-537); NaN passes through
 int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot, float* out,
-                   int64_t ldo, cudaStream_t st, float clamp = 0.f);
+                   int64_t ldo, cudaStream_t st, float clamp = 0.f, const float* smooth = nullptr);
 int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int rot, float* out_hi,
-                   float* out_lo, int64_t npad, int64_t ldo, cudaStream_t st);
+                   float* out_lo, int64_t npad, int64_t ldo, cudaStream_t st,
+                   const float* smooth = nullptr);
 int split_tf32(const float* in, int64_t rows, int64_t cols, int64_t ldi, float* hi, float* lo,
-               int64_t ldo, cudaStream_t st);
+               int64_t ldo, cudaStream_t st,
+               const float* smooth = nullptr);
 int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
             int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
             const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,

@@ -28,6 +28,14 @@ __global__ void __launch_bounds__(256) rotate_rows_kernel(const T* __restrict__ 
   store_row_smem(s, len, out + row * ldo + c0);
 }
 
+// torch semantics of (H / s_outer.clamp(min=1e-16)).clamp(max=1e30): NaN passes
+__device__ __forceinline__ float smooth_hessian(float h, float si, float sj) {
+  float p = __fmul_rn(sj, si);
+  p = p < 1e-16f ? 1e-16f : p;
+  const float q = __fdiv_rn(h, p);
+  return q > 1e30f ? 1e30f : q;
+}
+
 // Register-only row rotation for 16 <= rot <= 512: every warp streams groups
 // global -> registers -> butterflies -> global with no shared memory and no
 // barrier, 32/L groups per warp pass (L = rot/16 lanes per group, 16
@@ -38,7 +46,9 @@ template <typename T>
 __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ src, int64_t N, int64_t ld,
                                                           int64_t bstride, int64_t rows, int64_t valid, int64_t nb,
                                                           int rot, float* __restrict__ out, int64_t ldo,
-                                                          int64_t ostride, int64_t npad, float clamp) {
+                                                          int64_t ostride, int64_t npad, float clamp,
+                                                          const float* __restrict__ smw,
+                                                          const float* __restrict__ smh) {
   const int L = rot / 16, gpw = 32 / L;
   const int lane = threadIdx.x & 31, l = lane & (L - 1);
   const int64_t ngr = npad / rot;                    // groups per row
@@ -69,6 +79,17 @@ __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ 
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = fabsf(v[j]) > clamp ? 0.f : v[j];
     }
+    if (smw && act) {  // SmoothQuant: W[:, j] * s_j (smoothquant.py:54-69)
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (col + j < N) v[j] = __fmul_rn(v[j], smw[col + j]);
+    }
+    if (smh && act && r < valid) {  // H / max(s_i s_j, 1e-16), capped at 1e30 (pipeline.py:99-137)
+      const float si = smh[r];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (col + j < N) v[j] = smooth_hessian(v[j], si, smh[col + j]);
+    }
     hadamard_regs16(v, rot, l);
     if (act) {
       float* o = out + b * ostride + r * ldo + col;
@@ -87,11 +108,12 @@ __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ 
 template <typename T>
 void launch_rotate_regs(const T* src, int64_t N, int64_t ld, int64_t bstride, int64_t rows, int64_t valid,
                         int64_t nb, int rot, float* out, int64_t ldo, int64_t ostride, int64_t npad,
-                        cudaStream_t st, float clamp = 0.f) {
+                        cudaStream_t st, float clamp = 0.f, const float* smw = nullptr,
+                        const float* smh = nullptr) {
   const int64_t tasks = cdiv(nb * rows * (npad / rot), (int64_t)(32 / (rot / 16)));
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(tasks, 8), 148 * 16);
   rotate_regs_kernel<T><<<grid, 256, 0, st>>>(src, N, ld, bstride, rows, valid, nb, rot, out, ldo, ostride, npad,
-                                               clamp);
+                                               clamp, smw, smh);
 }
 
 // Row pass of R^T H R: every row of H gets the group Hadamard along its
@@ -194,12 +216,14 @@ __global__ void __launch_bounds__(512) hess_cols256_kernel(float* __restrict__ h
 }
 
 __global__ void split_kernel(const float* __restrict__ in, int64_t rows, int64_t cols, int64_t ldi,
-                             float* __restrict__ hi, float* __restrict__ lo, int64_t ldo) {
+                             float* __restrict__ hi, float* __restrict__ lo, int64_t ldo,
+                             const float* __restrict__ smh) {
   const int64_t total = rows * cols;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
-    const float v = in[r * ldi + c];
+    float v = in[r * ldi + c];
+    if (smh) v = smooth_hessian(v, smh[r], smh[c]);
     const float h = to_tf32(v);
     hi[r * ldo + c] = h;
     if (lo) lo[r * ldo + c] = __fsub_rn(v, h);
@@ -211,7 +235,7 @@ bool rot_ok(int rot) { return rot == 0 || (rot >= 2 && rot <= 1024 && (rot & (ro
 }  // namespace
 
 int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, int rot, float* out,
-                   int64_t ldo, cudaStream_t st, float clamp) {
+                   int64_t ldo, cudaStream_t st, float clamp, const float* smooth) {
   if (!rot_ok(rot)) return fail(IC_ERR_INVALID, "rot_size must be a power of 2, got %d", rot);
   if (M < 0 || N < 0 || ldw < N) return fail(IC_ERR_INVALID, "rotate_weights: bad shape");
   const int r = rot ? rot : 1;
@@ -221,16 +245,17 @@ int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, 
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_weights: too many rows");
   if (hadamard_regs_ok(r)) {
     switch (dtype) {
-      case IC_F32: launch_rotate_regs((const float*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp); break;
-      case IC_F16: launch_rotate_regs((const __half*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp); break;
+      case IC_F32: launch_rotate_regs((const float*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp, smooth); break;
+      case IC_F16: launch_rotate_regs((const __half*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp, smooth); break;
       case IC_BF16:
-        launch_rotate_regs((const __nv_bfloat16*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp);
+        launch_rotate_regs((const __nv_bfloat16*)W, N, ldw, 0, M, M, 1, r, out, ldo, 0, npad, st, clamp, smooth);
         break;
       default: return fail(IC_ERR_INVALID, "rotate_weights: unknown dtype %d", dtype);
     }
     IC_CHECK_LAUNCH();
     return IC_OK;
   }
+  if (smooth) return fail(IC_ERR_UNSUPPORTED, "rotate_weights: smoothing needs 16 <= rot_size <= 512");
   dim3 grid((unsigned)M, (unsigned)cdiv(npad, ROT_CHUNK));
   switch (dtype) {
     case IC_F32: rotate_rows_kernel<float><<<grid, 256, 0, st>>>((const float*)W, N, ldw, r, out, ldo, npad, clamp); break;
@@ -245,7 +270,7 @@ int rotate_weights(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, 
 }
 
 int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int rot, float* out_hi,
-                   float* out_lo, int64_t npad, int64_t ldo, cudaStream_t st) {
+                   float* out_lo, int64_t npad, int64_t ldo, cudaStream_t st, const float* smooth) {
   if (!rot_ok(rot)) return fail(IC_ERR_INVALID, "rot_size must be a power of 2, got %d", rot);
   const int r = rot ? rot : 1;
   if (nbatch < 1 || n <= 0 || ldh < n) return fail(IC_ERR_INVALID, "rotate_hessian: bad shape");
@@ -255,8 +280,10 @@ int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int r
     return fail(IC_ERR_INVALID, "Block size %lld is not divisible by rot_size %d", (long long)n, rot);
   if (npad > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rotate_hessian: too large");
   const int64_t ostride = npad * ldo;
+  if (smooth && (!hadamard_regs_ok(r) || nbatch != 1))
+    return fail(IC_ERR_UNSUPPORTED, "rotate_hessian: smoothing needs a 2-D Hessian and 16 <= rot_size <= 512");
   if (hadamard_regs_ok(r)) {
-    launch_rotate_regs(H, n, ldh, n * ldh, npad, n, nbatch, r, out_hi, ldo, ostride, npad, st);
+    launch_rotate_regs(H, n, ldh, n * ldh, npad, n, nbatch, r, out_hi, ldo, ostride, npad, st, 0.f, nullptr, smooth);
   } else {
     dim3 g1((unsigned)npad, (unsigned)cdiv(npad, ROT_CHUNK), (unsigned)nbatch);
     hess_rows_kernel<<<g1, 256, 0, st>>>(H, n, ldh, n * ldh, r, out_hi, npad, ldo, ostride);
@@ -280,11 +307,11 @@ int rotate_hessian(const float* H, int64_t nbatch, int64_t n, int64_t ldh, int r
 }
 
 int split_tf32(const float* in, int64_t rows, int64_t cols, int64_t ldi, float* hi, float* lo, int64_t ldo,
-               cudaStream_t st) {
+               cudaStream_t st, const float* smooth) {
   if (rows <= 0 || cols <= 0) return IC_OK;
   const int64_t total = rows * cols;
   const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 148 * 16);
-  split_kernel<<<blocks, 256, 0, st>>>(in, rows, cols, ldi, hi, lo, ldo);
+  split_kernel<<<blocks, 256, 0, st>>>(in, rows, cols, ldi, hi, lo, ldo, smooth);
   IC_CHECK_LAUNCH();
   return IC_OK;
 }

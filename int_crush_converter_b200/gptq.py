@@ -252,7 +252,7 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
                         asymmetric: bool = False, block_size: int = 128, damping: float = 0.01,
                         h_rotated: bool = False, want_codes: bool = False, want_packed: bool = True,
                         out: dict | None = None, ws: LayerWorkspace | None = None, check: bool = True,
-                        update_passes: int = 1) -> dict:
+                        update_passes: int = 1, smoothing: torch.Tensor | None = None) -> dict:
     """Fused GPTQ layer on the GPU: pipeline.py:527-559 + 702-809 + 919-931 + 1010-1013
     (outlier sanitize |w| > 1000 -> 0, rotations, GPTQ, packing, verify).
 
@@ -271,7 +271,10 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
     fp32 accumulation (default; the north star's "FP32-accumulate"), 3 =
     3xTF32.  The Hessian inverse is 3xTF32 either way.  Measured against the
     reference on the parity aggregates both keep tr((W-Q)H(W-Q)^T) within
-    0.15%.
+    0.15%.  ``smoothing`` (per-input-channel factors s, [in]) applies the
+    SmoothRot pre-step the pipeline runs on FFN down layers
+    (pipeline.py:547-553 + 766-774): W[:, j] * s_j and H[i, j] / (s_i s_j)
+    before both rotations, fused into their loads.
     """
     dev = device_of(W, H)
     Wd = W.to(dev)
@@ -302,7 +305,13 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
     lib = nat.load()
     need = lib.ic_gptq_layer_workspace_size(M, N, rot_size)
     wbuf = (ws or _default_ws).get(need, dev)
-    nat.check(lib.ic_gptq_layer(Wd.data_ptr(), _DT[Wd.dtype], M, N, N, Hd.data_ptr(), Hd.shape[1], int(h_rotated),
+    sm = None
+    if smoothing is not None:
+        sm = f32(smoothing, dev).reshape(-1).contiguous()
+        if sm.numel() != N:
+            raise ValueError(f"smoothing has {sm.numel()} factors for {N} input features")
+    nat.check(lib.ic_gptq_layer(Wd.data_ptr(), _DT[Wd.dtype], M, N, N, Hd.data_ptr(), Hd.shape[1], nat.ptr(sm),
+                                int(h_rotated),
                                 rot_size, int_bits, int(asymmetric), block_size, float(damping), int(update_passes),
                                 nat.ptr(codes),
                                 nat.ptr(packed), s16.data_ptr(), nat.ptr(zp), stats.data_ptr(), wbuf.data_ptr(),

@@ -821,3 +821,22 @@ def proxy_loss(W, Q, scales, zero_points, H) -> float:
         Qf = Qf - np.asarray(zero_points, np.float64).reshape(-1, 1)
     E = W - Qf * s
     return float(np.einsum("ij,ij->", E @ np.asarray(H, np.float64), E))
+
+
+# ---------------------------------------------------------------- SmoothRot pre-step
+def apply_smoothing_to_weight(W, s):  # smoothquant.py:54-69
+    """W[:, j] * s_j (fp32)."""
+    return (np.asarray(W, f32) * np.asarray(s, f32)[None, :]).astype(f32)
+
+
+SMOOTHQUANT_HESSIAN_FLOOR = f32(1e-8) * f32(1e-8)  # config.py:148-152
+SANITIZE_CEIL = f32(1e30)  # config.py:78
+
+
+def transform_hessian_for_smoothquant(H, s):  # pipeline.py:99-137 (2-D branch)
+    """H[i, j] / max(s_i s_j, 1e-16), capped at 1e30 (NaN passes)."""
+    s = np.asarray(s, f32)
+    outer = s[None, :] * s[:, None]
+    outer = np.where(outer < SMOOTHQUANT_HESSIAN_FLOOR, SMOOTHQUANT_HESSIAN_FLOOR, outer).astype(f32)
+    q = (np.asarray(H, f32) / outer).astype(f32)
+    return np.where(q > SANITIZE_CEIL, SANITIZE_CEIL, q).astype(f32)

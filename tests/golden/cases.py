@@ -95,6 +95,23 @@ PACK_CASES = {
     "pack_odd": dict(M=7, K=33, seed=92),
 }
 
+# SmoothRot pre-step (smoothquant.py:54-69, pipeline.py:99-137): the last two
+# factors are tiny so that s_i s_j hits the 1e-16 floor
+SMOOTH_CASES = {
+    "smooth_basic": dict(M=48, N=256, seed=95),
+}
+
+
+def smooth_inputs(case: dict):
+    M, N, seed = case["M"], case["N"], case["seed"]
+    W = gi.weight_outlier_cols(seed, M, N)
+    H = gi.hessian_lognormal(seed + 1, N, 2 * N)
+    rng = np.random.default_rng(seed + 2)
+    s = np.exp(rng.normal(0.0, 0.7, N)).astype(np.float32)
+    s[-2:] = np.float32(1e-9)
+    return W, H, s
+
+
 LINSPACE_CASES = {
     "ls_coarse_sym": (0.5, 2.0, 128),
     "ls_coarse_asym8": (0.8, 1.2, 128),

@@ -147,6 +147,13 @@ def main() -> None:
             put(name, scales=s, zp=zp)
         put(name, chk=gi.checksum(W, hd))
 
+    from converter import smoothquant
+    from converter import pipeline
+    for name, c in C.SMOOTH_CASES.items():
+        W, H, s = C.smooth_inputs(c)
+        put(name, W_smooth=smoothquant.apply_smoothing_to_weight(T(W), T(s)),
+            H_smooth=pipeline._transform_hessian_for_smoothquant(T(H), T(s)), chk=gi.checksum(W, H, s))
+
     np.savez_compressed(args.out, **out)
     print(f"wrote {len(out)} arrays to {args.out} ({os.path.getsize(args.out)} bytes)")
 

@@ -361,7 +361,7 @@ def test_gptq_layer_not_pd_reported():
     packed = torch.empty(M, N // 2, dtype=torch.uint8, device="cuda")
     s16 = torch.empty(M, dtype=torch.float16, device="cuda")
     zp = torch.empty(M, dtype=torch.int8, device="cuda")
-    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, 0, 256, 4, 0, 128, 0.01, 1, None,
+    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, None, 0, 256, 4, 0, 128, 0.01, 1, None,
                            packed.data_ptr(), s16.data_ptr(), zp.data_ptr(), None, ws.data_ptr(), ws.numel(),
                            nat.stream_ptr(W.device))
     assert st == nat.IC_ERR_NOT_PD
@@ -537,3 +537,28 @@ def test_fused_calls_sanitize_outliers_like_the_pipeline():
     assert np.array_equal(np_(rt["scales"]).reshape(-1), np.asarray(s_ref).reshape(-1))
     assert np.isfinite(np_(B.rotate_weights(cu(Ws), 256))).all()
     assert not np.isfinite(np_(B.rotate_weights(cu(W), 256))).all()  # the mirror keeps the reference's semantics
+
+
+def test_smoothing_mirrors_match_golden(golden):
+    W, H, s = C.smooth_inputs(C.SMOOTH_CASES["smooth_basic"])
+    assert np.array_equal(np_(B.apply_smoothing_to_weight(cu(W), cu(s))), golden["smooth_basic/W_smooth"])
+    assert np.array_equal(np_(B._transform_hessian_for_smoothquant(cu(H), cu(s))), golden["smooth_basic/H_smooth"])
+
+
+def test_gptq_layer_with_smoothrot_vs_oracle():
+    """The fused SmoothRot pre-step (W * s and H / (s_i s_j) in the rotation
+    loads) against the oracle's smooth -> rotate -> GPTQ."""
+    M, N = 256, 1024
+    W = gi.weight_outlier_cols(600, M, N)
+    H = gi.hessian_lognormal(601, N, 2 * N)
+    s = np.exp(np.random.default_rng(602).normal(0.0, 0.5, N)).astype(np.float32)
+    Wr = R.rotate_weights(R.apply_smoothing_to_weight(W, s), 256)
+    Hr = R.rotate_hessian(R.transform_hessian_for_smoothquant(H, s), 256)
+    ref = R.gptq_quantize_layer(Wr, Hr, 128, 0.01, 4)
+    out = B.quantize_gptq_layer(cu(W), cu(H), rot_size=256, want_codes=True,
+                                smoothing=cu(s))
+    q = np_(out["codes"])
+    assert np.array_equal(np_(out["scales"]), ref["scales"])
+    p = R.proxy_loss(Wr, q, ref["scales"].astype(np.float32), ref["zero_points"], Hr)
+    pr = R.proxy_loss(Wr, ref["quantized_W"], ref["scales"].astype(np.float32), ref["zero_points"], Hr)
+    assert abs(p / pr - 1) < 0.01, p / pr

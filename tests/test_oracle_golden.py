@@ -136,3 +136,10 @@ def test_piso(golden, name):
         assert np.array_equal(o[1], golden[name + "/zp"])
     else:
         assert np.array_equal(o, golden[name + "/scales"])
+
+
+@pytest.mark.parametrize("name", list(C.SMOOTH_CASES))
+def test_smoothing_matches_reference(golden, name):
+    W, H, s = C.smooth_inputs(C.SMOOTH_CASES[name])
+    assert np.array_equal(R.apply_smoothing_to_weight(W, s), golden[name + "/W_smooth"])
+    assert np.array_equal(R.transform_hessian_for_smoothquant(H, s), golden[name + "/H_smooth"])
