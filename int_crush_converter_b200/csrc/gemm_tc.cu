@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(384, 1)
 //             bytes, both CTAs' TMA loads complete_tx on it
 //   empty[s]  in each CTA; the MMA commit arrives on both (multicast mask 3)
 //   accf[b]   in each CTA; the MMA commit arrives on both
-//   acce[b]   leader only, 8 arrivals (4 epilogue warps x 2 CTAs)
+//   acce[b]   leader only, 16 arrivals (8 epilogue warps x 2 CTAs)
 // Each CTA's epilogue reads its own TMEM (its 128 rows).  All waits are
 // bounded; both CTAs always reach the closing cluster barrier.
 struct PairCfg {
