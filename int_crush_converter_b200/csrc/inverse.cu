@@ -67,6 +67,49 @@ __device__ __forceinline__ void put_pair(float* hi, float* lo, int64_t idx, floa
 constexpr int LDS = BASE + 1;
 constexpr size_t BASE_SMEM = (size_t)(2 * BASE * LDS + 3 * 32 * 33) * 4;
 
+// One diagonal of 32-blocks of Linv at distance D below the main one (4 - D
+// blocks, 2 (4 - D) elements per thread, every slot used):
+// X[I][J] = -X[I][I] * sum_{K=J}^{I-1} L[I][K] X[K][J], I = J + D.
+template <int D>
+__device__ __forceinline__ void offdiag_round(const float* a, float* x, float* tb, int tid) {
+  constexpr int NB = 4 - D, U = 2 * NB;
+  float acc[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) acc[u] = 0.f;
+#pragma unroll 4
+  for (int kk = 0; kk < 32 * D; ++kk) {  // T = sum_K L[I][K] X[K][J]
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = tid + 512 * u;
+      const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + D;
+      acc[u] = fmaf(a[(32 * I + rr) * LDS + 32 * J + kk], x[(32 * J + kk) * LDS + 32 * J + cc], acc[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int e = tid + 512 * u;
+    tb[(e >> 10) * 32 * 33 + ((e >> 5) & 31) * 33 + (e & 31)] = acc[u];
+    acc[u] = 0.f;
+  }
+  __syncthreads();
+#pragma unroll 4
+  for (int t = 0; t < 32; ++t) {  // X[I][J] = -X[I][I] T  (X[I][I] lower triangular)
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = tid + 512 * u;
+      const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + D;
+      if (t <= rr) acc[u] = fmaf(x[(32 * I + rr) * LDS + 32 * I + t], tb[J * 32 * 33 + t * 33 + cc], acc[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int e = tid + 512 * u;
+    const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + D;
+    x[(32 * I + rr) * LDS + 32 * J + cc] = -acc[u];
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, int n, int64_t ld, float* ihi,
                                                         float* ilo, unsigned* flags) {
   extern __shared__ float sm[];
@@ -74,6 +117,7 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
   float* x = sm + BASE * LDS;      // [128][LDS]  Linv
   float* tb = sm + 2 * BASE * LDS;  // [3][32][33] scratch blocks
   __shared__ int bad;
+  __shared__ float rdiag[32];  // 1 / L[p0+k][p0+k] of the current panel
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) bad = 0;
   if (n == BASE && (ld & 3) == 0 && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
@@ -107,25 +151,30 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
     // (1) 32 x 32 diagonal block, one warp: lane i holds row p0+i
     if (warp == 0) {
       float row[32];
-#pragma unroll
+#pragma unroll 32
       for (int j = 0; j < 32; ++j) row[j] = (j <= lane) ? a[(p0 + lane) * LDS + p0 + j] : 0.f;
-#pragma unroll
+#pragma unroll 32
       for (int k = 0; k < 32; ++k) {
         float d = __shfl_sync(0xffffffffu, row[k], k);
         if (!(d > 0.f) || !isfinite(d)) {
           if (lane == 0) bad = 1;
           d = 1.f;
         }
-        d = sqrtf(d);
-        const float l = (lane > k) ? __fdiv_rn(row[k], d) : (lane == k ? d : 0.f);
+        // 1/sqrt(d) from the hardware estimate refined by one Newton-Raphson
+        // step, r <- r (3 - d r^2) / 2: L[k][k] = d r and 1/L[k][k] = r, one
+        // serial operation per column instead of a square root and a division
+        float rd = rsqrtf(d);
+        rd = __fmul_rn(rd, __fmaf_rn(-0.5f * d, __fmul_rn(rd, rd), 1.5f));
+        if (lane == k) rdiag[k] = rd;
+        const float l = (lane > k) ? __fmul_rn(row[k], rd) : (lane == k ? __fmul_rn(d, rd) : 0.f);
         row[k] = l;
-#pragma unroll
+#pragma unroll 31
         for (int j = k + 1; j < 32; ++j) {
           const float lj = __shfl_sync(0xffffffffu, l, j);
           if (lane >= j) row[j] = fmaf(-l, lj, row[j]);
         }
       }
-#pragma unroll
+#pragma unroll 32
       for (int j = 0; j < 32; ++j)
         if (j <= lane) a[(p0 + lane) * LDS + p0 + j] = row[j];
     }
@@ -134,14 +183,14 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
     const int r = p0 + 32 + tid;
     if (r < BASE) {
       float xr[32];
-#pragma unroll
+#pragma unroll 32
       for (int k = 0; k < 32; ++k) {
         float s = a[r * LDS + p0 + k];
-#pragma unroll
+#pragma unroll 31
         for (int t = 0; t < k; ++t) s = fmaf(-xr[t], a[(p0 + k) * LDS + p0 + t], s);
-        xr[k] = __fdiv_rn(s, a[(p0 + k) * LDS + p0 + k]);
+        xr[k] = __fmul_rn(s, rdiag[k]);
       }
-#pragma unroll
+#pragma unroll 32
       for (int k = 0; k < 32; ++k) a[r * LDS + p0 + k] = xr[k];
     }
     __syncthreads();
@@ -149,7 +198,7 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
     for (int i = p0 + 32 + warp; i < BASE; i += 16) {
       for (int j = p0 + 32 + lane; j <= i; j += 32) {
         float s = a[i * LDS + j];
-#pragma unroll
+#pragma unroll 32
         for (int t = 0; t < 32; ++t) s = fmaf(-a[i * LDS + p0 + t], a[j * LDS + p0 + t], s);
         a[i * LDS + j] = s;
       }
@@ -160,60 +209,21 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
   if (warp < 4) {
     const int b0 = warp * 32, c = lane;
     float xc[32];
-#pragma unroll
+#pragma unroll 32
     for (int i = 0; i < 32; ++i) {
       float s = (i == c) ? 1.f : 0.f;
-#pragma unroll
+#pragma unroll 31
       for (int t = 0; t < i; ++t) s = fmaf(-a[(b0 + i) * LDS + b0 + t], xc[t], s);
       xc[i] = (i >= c) ? __fdiv_rn(s, a[(b0 + i) * LDS + b0 + i]) : 0.f;
     }
-#pragma unroll
+#pragma unroll 32
     for (int i = 0; i < 32; ++i) x[(b0 + i) * LDS + b0 + c] = xc[i];
   }
   __syncthreads();
   // off-diagonal blocks X[I][J] = -X[I][I] * sum_{K=J}^{I-1} L[I][K] X[K][J], by distance d = I - J
-  for (int d = 1; d < 4; ++d) {
-    const int nb = 4 - d;  // blocks on this diagonal; each thread owns up to 6 elements (independent chains)
-    float acc[6];
-#pragma unroll
-    for (int u = 0; u < 6; ++u) acc[u] = 0.f;
-    for (int kk = 0; kk < 32 * d; ++kk) {  // T = sum_K L[I][K] X[K][J]
-#pragma unroll
-      for (int u = 0; u < 6; ++u) {
-        const int e = tid + 512 * u;
-        if (e < nb * 1024) {
-          const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
-          acc[u] = fmaf(a[(32 * I + rr) * LDS + 32 * J + kk], x[(32 * J + kk) * LDS + 32 * J + cc], acc[u]);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 6; ++u) {
-      const int e = tid + 512 * u;
-      if (e < nb * 1024) tb[(e >> 10) * 32 * 33 + ((e >> 5) & 31) * 33 + (e & 31)] = acc[u];
-      acc[u] = 0.f;
-    }
-    __syncthreads();
-    for (int t = 0; t < 32; ++t) {  // X[I][J] = -X[I][I] T  (X[I][I] lower triangular)
-#pragma unroll
-      for (int u = 0; u < 6; ++u) {
-        const int e = tid + 512 * u;
-        if (e < nb * 1024) {
-          const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
-          if (t <= rr) acc[u] = fmaf(x[(32 * I + rr) * LDS + 32 * I + t], tb[J * 32 * 33 + t * 33 + cc], acc[u]);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 6; ++u) {
-      const int e = tid + 512 * u;
-      if (e < nb * 1024) {
-        const int J = e >> 10, rr = (e >> 5) & 31, cc = e & 31, I = J + d;
-        x[(32 * I + rr) * LDS + 32 * J + cc] = -acc[u];
-      }
-    }
-    __syncthreads();
-  }
+  offdiag_round<1>(a, x, tb, tid);
+  offdiag_round<2>(a, x, tb, tid);
+  offdiag_round<3>(a, x, tb, tid);
   for (int idx = tid; idx < BASE * BASE; idx += blockDim.x) {
     const int i = idx >> 7, j = idx & 127;
     if (i < n && j < n) put_pair(hi, lo, (int64_t)i * ld + j, (i >= j) ? a[i * LDS + j] : 0.f);
