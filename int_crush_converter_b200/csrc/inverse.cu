@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
   float* tb = sm + 2 * BASE * LDS;  // [3][32][33] scratch blocks
   __shared__ int bad;
   __shared__ float rdiag[32];  // 1 / L[p0+k][p0+k] of the current panel
+  __shared__ __align__(16) float colbuf[64];  // the panel's current column, double-buffered
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) bad = 0;
   if (n == BASE && (ld & 3) == 0 && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
@@ -168,9 +169,14 @@ __global__ void __launch_bounds__(512) chol_base_kernel(float* hi, float* lo, in
         if (lane == k) rdiag[k] = rd;
         const float l = (lane > k) ? __fmul_rn(row[k], rd) : (lane == k ? __fmul_rn(d, rd) : 0.f);
         row[k] = l;
+        // the column to every lane through shared memory (broadcast loads,
+        // vectorisable) rather than 31 - k shuffles; two buffers alternate
+        float* colk = colbuf + (k & 1) * 32;
+        colk[lane] = l;
+        __syncwarp();
 #pragma unroll 31
         for (int j = k + 1; j < 32; ++j) {
-          const float lj = __shfl_sync(0xffffffffu, l, j);
+          const float lj = colk[j];
           if (lane >= j) row[j] = fmaf(-l, lj, row[j]);
         }
       }
