@@ -239,6 +239,7 @@ def run_device(args, rank: int, world: int) -> None:
     phys = int(cvd.split(",")[local]) if cvd and cvd.split(",")[local].strip().isdigit() else local
     with ClockSampler(phys) as clk:
         l0 = lib.ic_launch_count()
+        g0 = lib.ic_inverse_graph_count()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         e0.record()
@@ -249,6 +250,7 @@ def run_device(args, rank: int, world: int) -> None:
         e1.record()
         torch.cuda.synchronize(dev)
         launches = lib.ic_launch_count() - l0
+        graphs = lib.ic_inverse_graph_count() - g0
     pool.check()
     if world > 1:
         torch.distributed.barrier()
@@ -278,6 +280,7 @@ def run_device(args, rank: int, world: int) -> None:
                        streams=args.streams),
         "e2e": e2e,
         "gpu_launches": int(launches),
+        "inverse_graphs_instantiated_in_timed_region": int(graphs),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": TRAFFIC_BYTES,
                      "kernel": "gemm_tn_kernel<128,3> (3xTF32), 16384^3 product of the mlp_down inverse, "

@@ -45,6 +45,10 @@ int ic_device_check(void);
 /* Number of kernels this library has launched in the process (all devices);
  * the benchmark uses it to count its own launches inside a timed region. */
 unsigned long long ic_launch_count(void);
+/* Number of Hessian-inverse CUDA graphs this library has instantiated in the
+ * process (each costs milliseconds of host time; a count that still grows in
+ * steady state means the replay cache misses). */
+unsigned long long ic_inverse_graph_count(void);
 /* Reads and clears the device status word (bit0 timeout, bit1 not-PD,
  * bit2 INT4 range).  Synchronises `stream`. */
 int ic_device_status(unsigned* flags_out, void* stream);

@@ -594,20 +594,26 @@ size_t layer_ws(int64_t M, int64_t N_in, int rot, LayerWs* out, void* base, size
   const int64_t ldw = round4(npad);
   Carver cv(base, cap);
   LayerWs w{};
-  w.W0 = cv.take<float>((size_t)M * ldw);
-  w.Wk = cv.take<float>((size_t)M * ldw);
+  // The Hessian pair, the status word and the inverse's scratch come first, at
+  // offsets that depend on the input width alone: the inverse's replayed graph
+  // is keyed on these addresses, so layers of one width that share a workspace
+  // (qkv, proj and mlp_up of a block) reuse one graph instead of instantiating
+  // one per output width (10-80 ms of host time each, during which no stream
+  // is fed).
   w.Hh = cv.take<float>((size_t)npad * ldw);
   w.Hl = cv.take<float>((size_t)npad * ldw);
+  w.status = cv.take<unsigned>(1);
+  w.inv_bytes = spd_inverse_ws(npad);
+  w.inv = cv.take<char>(w.inv_bytes);
+  w.W0 = cv.take<float>((size_t)M * ldw);
+  w.Wk = cv.take<float>((size_t)M * ldw);
   w.scale = cv.take<float>(M);
   w.zp = cv.take<float>(M);
   w.sscale = cv.take<float>(M);
   w.rmx = cv.take<float>(M);
   w.rsq = cv.take<double>(M);
-  w.status = cv.take<unsigned>(1);
   w.loop_bytes = loop_ws(M, npad, 128, LAYER_SB);
   w.loop = cv.take<char>(w.loop_bytes);
-  w.inv_bytes = spd_inverse_ws(npad);
-  w.inv = cv.take<char>(w.inv_bytes);
   if (out) *out = w;
   return cv.off + 256;
 }

@@ -450,6 +450,7 @@ constexpr size_t MAX_GRAPHS = 32;
 std::mutex g_graph_mu;
 std::vector<InvGraph> g_graphs;
 unsigned long long g_tick = 0;
+std::atomic<unsigned long long> g_instantiated{0};
 cudaStream_t g_capture[64] = {nullptr};
 
 bool graphs_enabled() {
@@ -481,7 +482,6 @@ int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_by
   if (!g_capture[key.dev]) IC_CUDA(cudaStreamCreateWithFlags(&g_capture[key.dev], cudaStreamNonBlocking));
   Ctx cc = c;
   cc.st = g_capture[key.dev];
-  const unsigned long long k0 = launches();
   IC_CUDA(cudaStreamBeginCapture(cc.st, cudaStreamCaptureModeThreadLocal));
   const int r = inverse_body(cc, n, damping, full);
   cudaGraph_t graph = nullptr;
@@ -492,12 +492,25 @@ int inverse_graph(const Ctx& c, int64_t n, float damping, void* ws, size_t ws_by
   }
   if (e != cudaSuccess || !graph)
     return fail(IC_ERR_CUDA, "spd_inverse: stream capture failed: %s", cudaGetErrorString(e));
+  // kernels in the graph (the library's launch counter also counts other host
+  // threads' launches made during the capture)
+  size_t nodes = 0;
+  unsigned long long kernels = 0;
+  if (cudaGraphGetNodes(graph, nullptr, &nodes) == cudaSuccess && nodes) {
+    std::vector<cudaGraphNode_t> list(nodes);
+    if (cudaGraphGetNodes(graph, list.data(), &nodes) == cudaSuccess)
+      for (size_t i = 0; i < nodes; ++i) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(list[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+      }
+  }
   cudaGraphExec_t exec = nullptr;
   const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
   if (ei != cudaSuccess) return fail(IC_ERR_CUDA, "spd_inverse: graph instantiation failed: %s", cudaGetErrorString(ei));
+  ++g_instantiated;
   key.exec = exec;
-  key.kernels = launches() - k0;  // counted while capturing; they run now, in the first replay
+  key.kernels = kernels;
   key.used = ++g_tick;
   if (g_graphs.size() >= MAX_GRAPHS) {
     size_t lru = 0;
@@ -558,3 +571,5 @@ extern "C" int ic_transpose(const float* in_hi, const float* in_lo, int64_t rows
                             float alpha, float* out_hi, float* out_lo, int64_t ldo, void* stream) {
   return ic::transpose(in_hi, in_lo, rows, cols, ldi, alpha, out_hi, out_lo, ldo, (cudaStream_t)stream);
 }
+
+extern "C" unsigned long long ic_inverse_graph_count(void) { return ic::g_instantiated.load(); }

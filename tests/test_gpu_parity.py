@@ -393,6 +393,37 @@ def test_gptq_layers_on_streams_match_serial():
             pool.submit(ins[1][0], -torch.eye(512, device="cuda"), rot_size=256)
 
 
+def test_layer_streams_callbacks_and_errors():
+    """Four lanes with pinned host inputs, twice through one pool: results match
+    the serial call, ``then`` runs on the lane's stream after the layer (a copy
+    to pinned host memory), and an invalid argument raises without leaving the
+    pool unusable."""
+    shapes = [(256, 1024), (512, 512), (128, 2048), (384, 1024), (256, 512), (512, 1024)]
+    ins = [(cu(gi.weight_outlier_cols(60 + i, m, n)).half(), cu(gi.hessian_lognormal(70 + i, n, 2 * n)))
+           for i, (m, n) in enumerate(shapes)]
+    serial = [B.quantize_gptq_layer(W, H, rot_size=256) for W, H in ins]
+    host = [torch.empty(r["packed"].shape, dtype=torch.uint8).pin_memory() for r in serial]
+    pool = B.LayerStreams(4)
+    for _ in range(2):
+        for h in host:
+            h.zero_()
+        with pool:
+            par = [pool.submit(W.cpu().pin_memory(), H.cpu().pin_memory(), rot_size=256,
+                               then=lambda o, h=h: h.copy_(o["packed"], non_blocking=True))
+                   for (W, H), h in zip(ins, host)]
+        torch.cuda.synchronize()
+        for a, b, h in zip(serial, par, host):
+            assert torch.equal(a["packed"], b["packed"])
+            assert torch.equal(a["stats"], b["stats"])
+            assert torch.equal(a["packed"].cpu(), h)
+    with pytest.raises(ValueError, match="int_bits"):
+        with pool:
+            pool.submit(*ins[0], rot_size=256, int_bits=5)
+    with pool:
+        again = pool.submit(*ins[1], rot_size=256)
+    assert torch.equal(again["packed"], serial[1]["packed"])
+
+
 # ---------------------------------------------------------------- LDLQ / greedy / PiSO
 @pytest.mark.parametrize("name", list(C.LDLQ_CASES))
 def test_ldlq(golden, name):
