@@ -250,8 +250,12 @@ __device__ __forceinline__ float code_arg(float v, float s, float rs, float z, b
   const float q0 = __fmul_rn(v, rs);
   const float q = __fmaf_rn(__fmaf_rn(-q0, s, v), rs, q0);
   float y = has_z ? __fadd_rn(q, z) : q;
+  // The corrected quotient is within an ulp of RN(v / s); a margin of 2^-14
+  // around the boundaries covers that up to |y| < 512 (ulp <= 2^-15), past
+  // every code of INT4 and INT8 (also with a zero-point), so only quotients
+  // that clamp to the end of the range anyway skip the check.
   const float a = fabsf(y);
-  if (a < 64.f) {
+  if (a < 512.f) {
     const float t = __fadd_rn(a, 0.5f);
     const float d = __fsub_rn(t, floor_small(t));
     if (d < 0x1p-14f || d > 1.f - 0x1p-14f) {
