@@ -57,6 +57,7 @@ struct BlockArgs {
   double* row_sqerr;
   float* row_maxerr;
   int vec;  // W and Hinv rows of this block are 16-byte aligned
+  unsigned* flags;  // device status word (DEV_TIMEOUT if a bounded wait gives up)
 };
 
 // Packed pairs of fp32 (low = first) and the sm_100 two-wide fp32 operations;
@@ -80,9 +81,48 @@ __device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
   return r;
 }
 
+// Bulk global -> shared copies (cp.async.bulk, no multicast) completing on an
+// mbarrier, and a bounded wait on it.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "{\n .reg .u64 g;\n cvta.to.global.u64 g, %1;\n"
+      " cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [g], %2, [%3];\n}\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, unsigned* flags) {
+  constexpr unsigned long long LIMIT_NS = 1000000000ull;  // 1 s
+  unsigned long long t0 = 0;
+  for (int spin = 0;; ++spin) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    unsigned long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (spin == 0) t0 = now;
+    else if (now - t0 > LIMIT_NS) {
+      if (flags) atomicOr(flags, DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Compact Hinv block: row j keeps columns [32*(j/32), 128) only (the serial
 // part reads its group's diagonal block, the apply part the columns after it).
 constexpr int HS_FLOATS = GROUP * (MAXB + (MAXB - GROUP) + (MAXB - 2 * GROUP) + (MAXB - 3 * GROUP));
+// weight staging row stride: 132 floats = 528 bytes, so the float4 accesses of
+// a quarter-warp (8 threads, 8 different rows) fall in 8 different 16-byte
+// bank groups
+constexpr int WLD = MAXB + 4;
+constexpr uint32_t BULK_BYTES = (uint32_t)(ROWS * MAXB * 4 + 2 * HS_FLOATS * 4);
 __device__ __forceinline__ int hs_index(int j, int c) {
   const int G = j >> 5;
   const int base = GROUP * (MAXB * G - 16 * G * (G - 1));  // sum of the earlier groups' rows
@@ -91,12 +131,14 @@ __device__ __forceinline__ int hs_index(int j, int c) {
 
 template <bool LDLQ>
 __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   // Hinv block (exact fp32), row j = error column j, compact: only columns from
   // the start of row j's group on are ever read (HS_FLOATS = 32 x (128+96+64+32))
   float* hs = smem;
-  float* wsm = hs + HS_FLOATS;      // [MAXB-GROUP][ROWS] weights of groups 1..3, column-major
-  float* dinv = wsm + (MAXB - GROUP) * ROWS;  // [MAXB] LDLQ: 1/max(Hinv[j,j],1e-8)
+  float* wst = hs + HS_FLOATS;            // [ROWS][WLD] the CTA's weight rows of the block, row-major
+  float* lost = wst + ROWS * WLD;         // lo halves of the compact Hinv block (bulk path)
+  float* dinv = lost + HS_FLOATS;         // [MAXB] LDLQ: 1/max(Hinv[j,j],1e-8)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(dinv + MAXB);
 
   const int t = threadIdx.x;
   const int bc = a.bc;
@@ -105,44 +147,34 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
   const int64_t rr = rv ? r : a.M - 1;  // clamp loads for the tail rows
 
   if (a.vec && bc == MAXB) {
-    // full 128 x 128 block: float4 loads, 8 in flight per thread
-    const float* hb = a.h_hi + a.i1 * a.ldh + a.i1;
-    const float* lb = a.h_lo + a.i1 * a.ldh + a.i1;
-#pragma unroll 1
-    for (int it = 0; it < MAXB * MAXB / 4 / ROWS; it += 8) {
-      float4 hv[8], lv[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int idx = (it + u) * ROWS + t;
-        const int j = idx >> 5, k4 = (idx & 31) << 2;
-        hv[u] = *reinterpret_cast<const float4*>(hb + j * a.ldh + k4);
-        lv[u] = *reinterpret_cast<const float4*>(lb + j * a.ldh + k4);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int idx = (it + u) * ROWS + t;
-        const int j = idx >> 5, k4 = (idx & 31) << 2;
-        if (k4 >= (j & ~(GROUP - 1)))
-          *reinterpret_cast<float4*>(hs + hs_index(j, k4)) =
-              make_float4(__fadd_rn(hv[u].x, lv[u].x), __fadd_rn(hv[u].y, lv[u].y),
-                          __fadd_rn(hv[u].z, lv[u].z), __fadd_rn(hv[u].w, lv[u].w));
-      }
+    // full 128 x 128 block: every byte in flight at once as bulk copies, one
+    // weight row and one compact Hinv row (hi and lo) per thread, all
+    // completing on one mbarrier; then hi + lo summed in place
+    const uint32_t mb = smem_addr(bar);
+    if (t == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mb));
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb), "r"(BULK_BYTES)
+                   : "memory");
     }
-    // this row's weights of groups 1..3 (group 0 goes to registers later), 8 float4 loads in flight
-    const float4* wrow = reinterpret_cast<const float4*>(a.W + rr * a.ldw + a.i1);
-#pragma unroll 1
-    for (int c4 = GROUP / 4; c4 < MAXB / 4; c4 += 8) {
-      float4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = wrow[c4 + u];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int c = 4 * (c4 + u) - GROUP;
-        wsm[c * ROWS + t] = v[u].x;
-        wsm[(c + 1) * ROWS + t] = v[u].y;
-        wsm[(c + 2) * ROWS + t] = v[u].z;
-        wsm[(c + 3) * ROWS + t] = v[u].w;
-      }
+    __syncthreads();
+    bulk_g2s(smem_addr(wst + t * WLD), a.W + rr * a.ldw + a.i1, MAXB * 4, mb);
+    const int c0 = (t >> 5) * GROUP;
+    const int64_t ho = (a.i1 + t) * a.ldh + a.i1 + c0;
+    const uint32_t len = (uint32_t)(MAXB - c0) * 4;
+    bulk_g2s(smem_addr(hs + hs_index(t, c0)), a.h_hi + ho, len, mb);
+    bulk_g2s(smem_addr(lost + hs_index(t, c0)), a.h_lo + ho, len, mb);
+    bool ok = bar_wait(mb, 0, a.flags);
+    if (!__syncthreads_and(ok)) {
+      if (!ok) bar_wait(mb, 0, nullptr);  // give the copies in flight (bounded) time to land
+      return;
+    }
+    float4* h4 = reinterpret_cast<float4*>(hs);
+    const float4* l4 = reinterpret_cast<const float4*>(lost);
+#pragma unroll 4
+    for (int i = t; i < HS_FLOATS / 4; i += ROWS) {
+      const float4 h = h4[i], l = l4[i];
+      h4[i] = make_float4(__fadd_rn(h.x, l.x), __fadd_rn(h.y, l.y), __fadd_rn(h.z, l.z), __fadd_rn(h.w, l.w));
     }
   } else {
     for (int j = 0; j < bc; ++j)
@@ -151,7 +183,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
         hs[hs_index(j, k)] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
       }
     const float* wrow = a.W + rr * a.ldw + a.i1;
-    for (int c = GROUP; c < bc; ++c) wsm[(c - GROUP) * ROWS + t] = wrow[c];
+    for (int c = 0; c < bc; ++c) wst[t * WLD + c] = wrow[c];
   }
   __syncthreads();
   if (LDLQ)
@@ -174,25 +206,20 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
     const int hstride = MAXB - cb;
     float w[GROUP], ev[GROUP];
     float sc[LDLQ ? GROUP : 1];
-    if (G == 0) {
-      const float* wrow = a.W + rr * a.ldw + a.i1;
-      if (a.vec && bc >= GROUP) {
+    {
+      const float4* wr = reinterpret_cast<const float4*>(wst + t * WLD + cb);
 #pragma unroll
-        for (int c4 = 0; c4 < GROUP / 4; ++c4) {
-          const float4 q4 = reinterpret_cast<const float4*>(wrow)[c4];
-          w[4 * c4] = q4.x;
-          w[4 * c4 + 1] = q4.y;
-          w[4 * c4 + 2] = q4.z;
-          w[4 * c4 + 3] = q4.w;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < GROUP; ++c) w[c] = (c < bc) ? wrow[c] : 0.f;
+      for (int c4 = 0; c4 < GROUP / 4; ++c4) {
+        const float4 q4 = wr[c4];
+        w[4 * c4] = q4.x;
+        w[4 * c4 + 1] = q4.y;
+        w[4 * c4 + 2] = q4.z;
+        w[4 * c4 + 3] = q4.w;
       }
     }
 #pragma unroll
     for (int c = 0; c < GROUP; ++c) {
-      if (G > 0) w[c] = (cb + c < bc) ? wsm[(cb + c - GROUP) * ROWS + t] : 0.f;
+      if (cb + c >= bc) w[c] = 0.f;  // columns past a ragged block's end (unset staging)
       if (LDLQ) sc[c] = (cb + c < bc) ? fmaxf(a.scale2d[rr * a.lds + a.i1 + cb + c], 1e-8f) : 1.f;
     }
     // the group's columns in order, each error applied at once to the group's later columns
@@ -319,9 +346,10 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
     const int cend = (bc + 3) & ~3;  // columns past bc are scratch (never read back)
 #pragma unroll 1
     for (int c2 = cb + GROUP; c2 < cend; c2 += 4) {
-      float* wc = wsm + (c2 - GROUP) * ROWS + t;
+      float4* wc = reinterpret_cast<float4*>(wst + t * WLD + c2);
       // two columns per packed f32x2 operation (each half rounded as the scalar op)
-      uint64_t v01 = pack2(wc[0], wc[ROWS]), v23 = pack2(wc[2 * ROWS], wc[3 * ROWS]);
+      const float4 w4 = *wc;
+      uint64_t v01 = pack2(w4.x, w4.y), v23 = pack2(w4.z, w4.w);
 #pragma unroll
       for (int j = 0; j < GROUP; ++j) {
         const ulonglong2 h = *reinterpret_cast<const ulonglong2*>(hg + j * hstride + (c2 - cb));
@@ -329,8 +357,10 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
         v01 = sub_f32x2(v01, mul_f32x2(e2, h.x));
         v23 = sub_f32x2(v23, mul_f32x2(e2, h.y));
       }
-      unpack2(v01, wc[0], wc[ROWS]);
-      unpack2(v23, wc[2 * ROWS], wc[3 * ROWS]);
+      float4 o4;
+      unpack2(v01, o4.x, o4.y);
+      unpack2(v23, o4.z, o4.w);
+      *wc = o4;
     }
   }
   if (want_stats && rv) {
@@ -339,7 +369,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(const BlockArgs a) {
   }
 }
 
-constexpr size_t BLOCK_SMEM = (size_t)HS_FLOATS * 4 + (size_t)(MAXB - GROUP) * ROWS * 4 + MAXB * 4;
+constexpr size_t BLOCK_SMEM = (size_t)HS_FLOATS * 4 * 2 + (size_t)ROWS * WLD * 4 + MAXB * 4 + 16;
 
 // ---- per-row scale / zero-point preparation (converter/gptq.py:254-317) ----
 __global__ void __launch_bounds__(256) row_params_kernel(const float* __restrict__ W, int64_t N, int64_t ldw,
@@ -512,6 +542,8 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (L.ldh % 4) return fail(IC_ERR_INVALID, "Hinv leading dimension must be a multiple of 4");
   if (L.packed && (L.B % 2)) return fail(IC_ERR_UNSUPPORTED, "in-loop packing needs an even block size");
   if (ws_bytes < loop_ws(L.M, L.N, L.B, L.SB)) return fail(IC_ERR_WORKSPACE, "gptq: workspace too small");
+  unsigned* flags = device_flags();
+  if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
   const int SB = (L.B % 4) ? L.B : L.SB;
   const int64_t lde = (SB + 3) & ~3;
   Carver cv(ws, ws_bytes);
@@ -552,6 +584,7 @@ int run_loop(const LoopArgs& L, void* ws, size_t ws_bytes, cudaStream_t st) {
       a.lde = lde; a.row_sqerr = L.row_sqerr; a.row_maxerr = L.row_maxerr;
       a.vec = ((L.ldw | L.ldh | i1) & 3) == 0 && (reinterpret_cast<uintptr_t>(L.W) & 15) == 0 &&
               (reinterpret_cast<uintptr_t>(L.h_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(L.h_lo) & 15) == 0;
+      a.flags = flags;
       if (L.ldlq) block_kernel<true><<<nblk, ROWS, BLOCK_SMEM, st>>>(a);
       else block_kernel<false><<<nblk, ROWS, BLOCK_SMEM, st>>>(a);
       IC_CHECK_LAUNCH();
