@@ -49,6 +49,13 @@ unsigned long long ic_launch_count(void);
  * process (each costs milliseconds of host time; a count that still grows in
  * steady state means the replay cache misses). */
 unsigned long long ic_inverse_graph_count(void);
+/* Failure-path self-test (no reference counterpart): launches one thread that
+ * waits on an mbarrier nothing arrives on, through the same bounded wait every
+ * kernel of the library uses; after `limit_ns` (0.1 ms .. 2 s) it gives up,
+ * sets DEV_TIMEOUT in the device status word (read it with
+ * ic_device_status) and returns, leaving the context usable.  Asynchronous
+ * on `stream`. */
+int ic_selftest_bounded_wait(unsigned long long limit_ns, void* stream);
 /* Reads and clears the device status word (bit0 timeout, bit1 not-PD,
  * bit2 INT4 range).  Synchronises `stream`. */
 int ic_device_status(unsigned* flags_out, void* stream);

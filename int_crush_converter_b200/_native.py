@@ -43,6 +43,7 @@ SIGNATURES = {
     "ic_device_check": (_i32, []),
     "ic_launch_count": (ctypes.c_ulonglong, []),
     "ic_inverse_graph_count": (ctypes.c_ulonglong, []),
+    "ic_selftest_bounded_wait": (_i32, [ctypes.c_ulonglong, _vp]),
     "ic_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _vp]),
     "ic_rotate_weights": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _vp, _i64, _vp]),
     "ic_rotate_hessian": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _vp]),

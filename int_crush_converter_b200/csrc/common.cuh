@@ -73,6 +73,35 @@ unsigned long long launches();
 enum : unsigned { DEV_TIMEOUT = 1u, DEV_NOT_PD = 2u, DEV_RANGE = 4u };
 unsigned* device_flags();  // per-device word, allocated once at first use
 
+// Bounded wait on phase `parity` of a shared-memory mbarrier: true once the
+// phase completed; false after `limit_ns` of globaltimer time, with
+// DEV_TIMEOUT or-ed into *flags (if given).  Every mbarrier wait of the
+// library goes through this, so no kernel can spin forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned* flags,
+                                                  unsigned long long limit_ns) {
+  unsigned long long t0 = 0;
+  for (int spin = 0;; ++spin) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((spin & 255) == 0) {
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (spin == 0) {
+        t0 = now;
+      } else if (now - t0 > limit_ns) {
+        if (flags) atomicOr(flags, DEV_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // ---- reference rounding ---------------------------------------------------------

@@ -47,11 +47,6 @@ struct GemmArgs {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
@@ -59,28 +54,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 // Bounded wait: returns false (and flags a timeout) instead of spinning forever.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned* flags) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (;;) {
-    for (int i = 0; i < 256; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
-      atomicOr(flags, DEV_TIMEOUT);
-      return false;
-    }
-  }
+  return mbar_wait_bounded(bar, parity, flags, WAIT_LIMIT_NS);
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y,
                                             uint32_t bar) {
@@ -913,6 +889,30 @@ extern "C" int ic_gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const fl
                           float* d_hi, float* d_lo, int64_t ldd, int passes, void* stream) {
   return ic::gemm_tn(m, n, k, alpha, a_hi, a_lo, lda, b_hi, b_lo, ldb, beta, c_hi, c_lo, ldc, d_hi, d_lo,
                      ldd, passes, static_cast<cudaStream_t>(stream));
+}
+
+namespace ic {
+namespace {
+// One thread waits on an mbarrier that nothing arrives on: the library's
+// bounded wait must give up after limit_ns, record DEV_TIMEOUT and return.
+__global__ void wait_selftest_kernel(unsigned* flags, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  mbar_init(b, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  mbar_wait_bounded(b, 0, flags, limit_ns);
+}
+}  // namespace
+}  // namespace ic
+
+extern "C" int ic_selftest_bounded_wait(unsigned long long limit_ns, void* stream) {
+  if (limit_ns < 100000ull || limit_ns > 2000000000ull)
+    return ic::fail(IC_ERR_INVALID, "selftest wait limit must be in [0.1 ms, 2 s]");
+  unsigned* flags = ic::device_flags();
+  if (!flags) return ic::fail(IC_ERR_CUDA, "device status word unavailable");
+  ic::wait_selftest_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(flags, limit_ns);
+  IC_CHECK_LAUNCH();
+  return IC_OK;
 }
 
 extern "C" int ic_gemm_tn_tri(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi,

@@ -94,25 +94,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, unsigned* flags) {
-  constexpr unsigned long long LIMIT_NS = 1000000000ull;  // 1 s
-  unsigned long long t0 = 0;
-  for (int spin = 0;; ++spin) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    unsigned long long now;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-    if (spin == 0) t0 = now;
-    else if (now - t0 > LIMIT_NS) {
-      if (flags) atomicOr(flags, DEV_TIMEOUT);
-      return false;
-    }
-  }
+  return mbar_wait_bounded(bar, parity, flags, 1000000000ull);  // 1 s
 }
 
 // Compact Hinv block: row j keeps columns [32*(j/32), 128) only (the serial

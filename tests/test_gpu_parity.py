@@ -424,6 +424,31 @@ def test_layer_streams_callbacks_and_errors():
     assert torch.equal(again["packed"], serial[1]["packed"])
 
 
+def test_bounded_wait_times_out_and_context_survives():
+    """Failure path without a GPU fault: a kernel waits on an mbarrier that
+    nothing arrives on through the library's bounded wait; after the limit it
+    records DEV_TIMEOUT in the device status word and returns, the host reads
+    the bit, and the context runs a parity-checked call afterwards."""
+    import ctypes
+    lib = nat.load()
+    st = nat.stream_ptr(torch.device("cuda", 0))
+    f = ctypes.c_uint(0)
+    nat.check(lib.ic_device_status(ctypes.byref(f), st))  # clear
+    with pytest.raises(ValueError):
+        nat.check(lib.ic_selftest_bounded_wait(10, st))
+    nat.check(lib.ic_selftest_bounded_wait(20_000_000, st))  # 20 ms
+    nat.check(lib.ic_device_status(ctypes.byref(f), st))
+    assert f.value & nat.DEV_TIMEOUT
+    nat.check(lib.ic_device_status(ctypes.byref(f), st))
+    assert f.value == 0  # read-and-clear
+    W, H = cu(gi.weight_outlier_cols(80, 256, 512)).half(), cu(gi.hessian_lognormal(81, 512, 1024))
+    a = B.quantize_gptq_layer(W, H, rot_size=256)
+    b = B.quantize_gptq_layer(W, H, rot_size=256)
+    assert torch.equal(a["packed"], b["packed"]) and int(a["stats"][2].item()) == 0
+    nat.check(lib.ic_device_status(ctypes.byref(f), st))
+    assert f.value == 0
+
+
 # ---------------------------------------------------------------- LDLQ / greedy / PiSO
 @pytest.mark.parametrize("name", list(C.LDLQ_CASES))
 def test_ldlq(golden, name):
