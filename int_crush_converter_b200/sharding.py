@@ -83,3 +83,145 @@ def owners(names: Iterable[str], shapes: Sequence[tuple[int, int]], world: int) 
     table = shard_layers([layer_cost(m, n) for m, n in shapes], world)
     names = list(names)
     return {names[i]: r for r, idx in enumerate(table) for i in idx}
+
+
+# ---------------------------------------------------------------------------
+# Row sharding of one layer.  Given H^-1, GPTQ's rows are independent: the
+# column loop (rounding.py:37-103) and the lazy update W[:, after] -= E Hinv
+# act row by row and the scales / zero-points are per row (gptq.py:254-317).
+# So one rank inverts the damped Hessian, broadcasts the H^-1 pair (NCCL over
+# NVLink; 2 x 1 GiB at N = 16384), every rank runs its contiguous share of the
+# rows, and the codes, scales and zero-points are all-gathered.  Results are
+# identical to the one-GPU layer: each output element of the trailing-update
+# GEMM sums the same K chunks in the same order whatever the row tiling.  The
+# inverse itself (most of an mlp_down layer's flops) is not sharded, so this
+# pays off only to balance the tail of a layer-sharded job.
+
+def row_slice(rows: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous balanced share [r0, r1) of `rows` for `rank`."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of size {world}")
+    return rows * rank // world, rows * (rank + 1) // world
+
+
+def _group_info(group) -> tuple[int, int]:
+    if not (torch.distributed.is_available() and torch.distributed.is_initialized()):
+        return 0, 1
+    return torch.distributed.get_rank(group), torch.distributed.get_world_size(group)
+
+
+def gather_rows(local: torch.Tensor, rows: int, group=None) -> torch.Tensor:
+    """All-gather each rank's row slice (``row_slice`` of `rows`) into the full
+    [rows, ...] tensor on every rank (slices padded to a common size)."""
+    rank, world = _group_info(group)
+    if world == 1:
+        return local
+    pad = -(-rows // world)
+    buf = torch.zeros((pad,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    buf[:local.shape[0]] = local
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    torch.distributed.all_gather(parts, buf, group=group)
+    out = []
+    for r, p in enumerate(parts):
+        r0, r1 = row_slice(rows, r, world)
+        out.append(p[:r1 - r0])
+    return torch.cat(out, 0)
+
+
+def reduce_row_stats(sq: torch.Tensor, mx: torch.Tensor, group=None) -> tuple[float, float]:
+    """Sum of the ranks' squared errors (fp64) and max of their max errors."""
+    rank, world = _group_info(group)
+    sq = sq.reshape(1).to(torch.float64).clone()
+    mx = mx.reshape(1).to(torch.float32).clone()
+    if world > 1:
+        torch.distributed.all_reduce(sq, op=torch.distributed.ReduceOp.SUM, group=group)
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX, group=group)
+    return float(sq.item()), float(mx.item())
+
+
+def _quantize_rows(Wd: torch.Tensor, hi: torch.Tensor, lo: torch.Tensor, r0: int, r1: int, block_size: int,
+                   int_bits: int, asymmetric: bool):
+    """GPTQ over rows [r0, r1) of the fp32 device weight `Wd` given the H^-1
+    pair: (codes int8, scale f32, zp f32 or None, sum of squared errors fp64,
+    max error f32) for those rows."""
+    from . import _native as nat
+    from .gptq import _run_loop
+    dev = Wd.device
+    N = Wd.shape[1]
+    qmin, qmax = (-128, 127) if int_bits == 8 else (-8, 7)
+    Wl = Wd[r0:r1].contiguous()
+    m = Wl.shape[0]
+    scale = torch.empty(m, dtype=torch.float32, device=dev)
+    zp = torch.empty(m, dtype=torch.float32, device=dev) if (int_bits == 4 or asymmetric) else None
+    Q = torch.zeros(m, N, dtype=torch.int8, device=dev)
+    if m == 0 or N == 0:
+        z = torch.zeros((), dtype=torch.float64, device=dev)
+        return Q, scale, zp, z, z.float()
+    lib = nat.load()
+    nat.check(lib.ic_gptq_row_params(Wl.data_ptr(), m, N, N, int_bits, int(asymmetric), scale.data_ptr(),
+                                     nat.ptr(zp), nat.stream_ptr(dev)), "gptq_row_params")
+    rsq, rmx = _run_loop(Wl.clone(), Wl, 0, N, hi, lo, hi.shape[1], block_size, scale, zp, qmin, qmax, Q)
+    return Q, scale, zp, rsq.sum(), rmx.max()
+
+
+def gptq_quantize_layer_row_sharded(W: torch.Tensor, hessian: torch.Tensor, group=None, src: int = 0,
+                                    block_size: int = 128, damping: float = 0.01, int_bits: int = 4,
+                                    asymmetric: bool = False):
+    """:func:`~int_crush_converter_b200.gptq.gptq_quantize_layer` (gptq.py:137-417,
+    dense 2-D Hessian) with the rows of one layer spread over the process
+    group: rank `src` (group rank) inverts the damped Hessian on its GPU and
+    broadcasts the H^-1 pair; every rank quantizes its ``row_slice``; every rank
+    returns the full :class:`QuantizationResult`.  Call it on every rank with
+    the same W and H.  Without an initialised process group it is the one-GPU
+    layer."""
+    from ._dev import back, device_of, f32, round4
+    from .config import SCALE_DTYPE
+    from .hessian import hessian_pair, inverse_pair
+    from .types import QuantizationResult
+    if int_bits not in (4, 8):
+        raise ValueError(f"int_bits must be 4 or 8, got {int_bits}")
+    if W.dim() != 2:
+        raise ValueError(f"Expected 2D weight tensor, got {W.dim()}D")
+    if not isinstance(hessian, torch.Tensor) or hessian.dim() != 2:
+        raise ValueError("row sharding takes a dense 2-D Hessian")
+    rank, world = _group_info(group)
+    if not 0 <= src < world:
+        raise ValueError(f"src {src} outside group of size {world}")
+    dev = device_of(W, hessian)
+    Wd = f32(W, dev)
+    M, N = Wd.shape
+    if tuple(hessian.shape) != (N, N):
+        raise ValueError(f"Hessian shape {tuple(hessian.shape)} != ({N}, {N})")
+    paths = ("cholesky", "inv", "pinv")
+    if rank == src:
+        Hd = f32(hessian, dev)
+        hi, lo, n = hessian_pair(Hd, 0, dev, rotate=False)
+        path = inverse_pair(hi, lo, n, damping, H_fallback=Hd)
+    else:
+        hi = torch.empty(N, round4(N), dtype=torch.float32, device=dev)
+        lo = torch.empty_like(hi)
+        path = paths[0]
+    if world > 1:
+        g_src = torch.distributed.get_global_rank(group, src) if group is not None else src
+        code = torch.tensor([paths.index(path)], dtype=torch.int32, device=dev)
+        torch.distributed.broadcast(code, g_src, group=group)
+        torch.distributed.broadcast(hi, g_src, group=group)
+        torch.distributed.broadcast(lo, g_src, group=group)
+        path = paths[int(code.item())]
+    r0, r1 = row_slice(M, rank, world)
+    Q, scale, zp, sq, mx = _quantize_rows(Wd, hi, lo, r0, r1, block_size, int_bits, asymmetric)
+    Q = gather_rows(Q, M, group)
+    scale = gather_rows(scale, M, group)
+    zp = gather_rows(zp, M, group) if zp is not None else None
+    sq, mx = reduce_row_stats(sq, mx, group)
+    mse = sq / (M * N) if M * N else 0.0
+    zp8 = None if zp is None else zp.reshape(M, 1).to(torch.int8)
+    return QuantizationResult(
+        quantized_W=back(Q, W),
+        scales=back(scale.reshape(M, 1).to(SCALE_DTYPE), W),
+        zero_points=back(zp8, W),
+        mse=mse,
+        max_err=mx if M * N else 0.0,
+        method_used="gptq_b200",
+        fallbacks=[] if path == "cholesky" else [f"hessian_{path}"],
+    )

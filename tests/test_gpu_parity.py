@@ -449,6 +449,37 @@ def test_bounded_wait_times_out_and_context_survives():
     assert f.value == 0
 
 
+@pytest.mark.parametrize("M,N,bits,asym", [(300, 512, 4, False), (257, 384, 8, False), (130, 256, 8, True)])
+def test_row_sharded_layer_equals_one_gpu(M, N, bits, asym):
+    """Row sharding of one layer: the rows quantized in slices against the same
+    H^-1 pair, concatenated, equal the one-GPU layer bit for bit (codes,
+    scales, zero-points); the public entry at world size 1 is the one-GPU
+    layer; a slice of no rows is handled."""
+    from int_crush_converter_b200 import sharding as S
+    from int_crush_converter_b200.hessian import hessian_pair, inverse_pair
+    W = cu(gi.weight_outlier_cols(90 + M, M, N))
+    H = cu(gi.hessian_lognormal(91 + N, N, 2 * N))
+    ref = B.gptq_quantize_layer(W, H, int_bits=bits, asymmetric=asym)
+    one = S.gptq_quantize_layer_row_sharded(W, H, int_bits=bits, asymmetric=asym)
+    assert torch.equal(one.quantized_W, ref.quantized_W)
+    assert torch.equal(one.scales, ref.scales)
+    assert (one.zero_points is None) == (ref.zero_points is None)
+    if ref.zero_points is not None:
+        assert torch.equal(one.zero_points, ref.zero_points)
+    assert one.mse == pytest.approx(ref.mse, rel=1e-12) and one.max_err == ref.max_err
+    hi, lo, n = hessian_pair(H, 0, W.device, rotate=False)
+    assert inverse_pair(hi, lo, n, 0.01, H_fallback=H) == "cholesky"
+    for world in (2, 3):
+        parts = [S._quantize_rows(W, hi, lo, *S.row_slice(M, r, world), 128, bits, asym) for r in range(world)]
+        assert torch.equal(torch.cat([p[0] for p in parts]), ref.quantized_W)
+        assert torch.equal(torch.cat([p[1] for p in parts]).half().reshape(M, 1), ref.scales)
+        sq = sum(float(p[3]) for p in parts)
+        assert sq / (M * N) == pytest.approx(ref.mse, rel=1e-12)
+        assert max(float(p[4]) for p in parts) == ref.max_err
+    empty = S._quantize_rows(W, hi, lo, 5, 5, 128, bits, asym)
+    assert empty[0].shape == (0, N) and float(empty[3]) == 0.0
+
+
 # ---------------------------------------------------------------- LDLQ / greedy / PiSO
 @pytest.mark.parametrize("name", list(C.LDLQ_CASES))
 def test_ldlq(golden, name):

@@ -80,3 +80,59 @@ def test_two_gloo_ranks_shard_disjointly_and_time_with_max():
     for r in res:
         assert r[2] == [mine0, mine1]
         assert r[3] == 11.0
+
+
+# ---------------------------------------------------------------- row sharding of one layer
+def test_row_slices_partition_the_rows():
+    for rows in (0, 1, 7, 4096, 12289):
+        for world in (1, 2, 3, 8):
+            sl = [S.row_slice(rows, r, world) for r in range(world)]
+            assert sl[0][0] == 0 and sl[-1][1] == rows
+            assert all(a[1] == b[0] for a, b in zip(sl, sl[1:]))
+            assert max(b - a for a, b in sl) - min(b - a for a, b in sl) <= 1
+    with pytest.raises(ValueError):
+        S.row_slice(8, 2, 2)
+
+
+def _row_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rows = 7
+        full = torch.arange(rows * 3, dtype=torch.float32).reshape(rows, 3)
+        codes = (torch.arange(rows * 5) % 16 - 8).to(torch.int8).reshape(rows, 5)
+        r0, r1 = S.row_slice(rows, rank, world)
+        g = S.gather_rows(full[r0:r1].clone(), rows)
+        gc = S.gather_rows(codes[r0:r1].clone(), rows)
+        sq, mx = S.reduce_row_stats(torch.tensor(1.5 + rank, dtype=torch.float64),
+                                    torch.tensor(float(rank), dtype=torch.float32))
+        q.put((rank, torch.equal(g, full), torch.equal(gc, codes), sq, mx))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_two_gloo_ranks_gather_row_slices_and_reduce_stats():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok_f, ok_c, sq, mx in res:
+        assert ok_f and ok_c
+        assert sq == 1.5 + 2.5 and mx == 1.0
+
+
+def test_row_sharded_validates_without_a_gpu():
+    W = torch.zeros(4, 8)
+    with pytest.raises(ValueError):
+        S.gptq_quantize_layer_row_sharded(W, torch.zeros(2, 8, 8))
+    with pytest.raises(ValueError):
+        S.gptq_quantize_layer_row_sharded(W, torch.eye(8), int_bits=3)
+    with pytest.raises(ValueError):
+        S.gptq_quantize_layer_row_sharded(W, torch.eye(8), src=1)
