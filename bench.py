@@ -131,26 +131,69 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ----------------------------------------------------------------------------- CPU (oracle) arm
+# ----------------------------------------------------------------------------- reference (CPU) arm
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _reference_converter():
+    """The unmodified reference package installed under baseline/_ref (pip --target),
+    with its Triton path switched off through its own switch (gptq.py:24) so that
+    it runs its CPU PyTorch code; None when it is not installed."""
+    os.environ["GPTQ_DISABLE_TRITON"] = "1"
+    if not os.path.isdir(os.path.join(REF_DIR, "converter")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import importlib
+    return {m: importlib.import_module(f"converter.{m}") for m in ("rotation", "gptq", "packing")}
+
+
+def cpu_layer_inputs(name: str, m: int, n: int, seed: int):
+    """Seeded CPU inputs of one layer with the bench's distributions (fp16-valued
+    W upcast to fp32 as pipeline.py:524 does; H = X^T X / 8192)."""
+    g = torch.Generator().manual_seed(seed)
+    W = (torch.randn(m, n, generator=g) * 0.02).half().float()
+    s = torch.exp(torch.randn(n, generator=g))
+    H = torch.zeros(n, n)
+    for c0 in range(0, N_SAMPLES, 2048):
+        X = torch.randn(min(2048, N_SAMPLES - c0), n, generator=g) * s
+        H.addmm_(X.T, X)
+    H.div_(N_SAMPLES)
+    return W, 0.5 * (H + H.T)
+
+
+def reference_layer_seconds(ref, W, H) -> float:
+    """One layer through the reference's own per-layer calls, as pipeline.py:547-559,
+    702-789 and 1010-1013 make them: rotate_weights -> rotate_hessian ->
+    gptq_quantize_layer -> pack_int4 (CPU tensors)."""
+    t0 = time.perf_counter()
+    Wr = ref["rotation"].rotate_weights(W, ROT)
+    Hr = ref["rotation"].rotate_hessian(H, ROT)
+    r = ref["gptq"].gptq_quantize_layer(Wr, Hr, block_size=BLOCK, damping=DAMP, int_bits=4)
+    ref["packing"].pack_int4(r.quantized_W)
+    return time.perf_counter() - t0
+
+
 def cpu_sample_seconds(reps: int = 1):
-    """Time the reference algorithm (oracle/cpu_ref.py, numpy + LAPACK on all host
-    cores) on the proj layer [4096, 4096] of a seeded set; returns (seconds/rep, params)."""
-    import numpy as np
+    """The reference's CPU path on the proj layer [4096, 4096] of a seeded set
+    (baseline/_ref when installed, else the oracle restatement); returns
+    (seconds per rep, params, kind)."""
+    name, m, n = LAYERS[1]
+    ref = _reference_converter()
+    if ref is not None:
+        W, H = cpu_layer_inputs(name, m, n, 4321)
+        return [reference_layer_seconds(ref, W, H) for _ in range(reps)], m * n, "reference"
     from oracle import cpu_ref as R
     from tests.golden import inputs as gi
-    name, m, n = LAYERS[1]
     W = gi.weight_outlier_cols(1234, m, n, frac=0.0005, mult=1.0)
     H = gi.hessian_lognormal(4321, n, N_SAMPLES)
     ts = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        Wr = R.rotate_weights(W, ROT)
-        Hr = R.rotate_hessian(H, ROT)
-        r = R.gptq_quantize_layer(Wr, Hr, BLOCK, DAMP, 4)
+        r = R.gptq_quantize_layer(R.rotate_weights(W, ROT), R.rotate_hessian(H, ROT), BLOCK, DAMP, 4)
         R.pack_int4(r["quantized_W"])
         ts.append(time.perf_counter() - t0)
-    del np
-    return ts, m * n
+    return ts, m * n, "port"
 
 
 def cpu_cores() -> int:
@@ -161,22 +204,45 @@ def cpu_cores() -> int:
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference's own CPU implementation on the B200 arm's config: one step =
+    one DiT linear set (qkv, proj, mlp_up, mlp_down) through its per-layer calls,
+    all host threads.  A set takes about a minute of CPU, so the timed steps stop
+    at --ref-budget seconds (after at least one whole set); `steps` reports the
+    sets actually timed.  Warm-up steps run the proj layer only."""
     if rank != 0:
         return
+    ref = _reference_converter()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref "
+                                                               "(pip install --target baseline/_ref)"}), flush=True)
+        return
+    torch.set_num_threads(cpu_cores())
+    inputs = {name: cpu_layer_inputs(name, m, n, 77 + i) for i, (name, m, n) in enumerate(LAYERS)}
     for _ in range(args.warmup):
-        cpu_sample_seconds(1)
-    ts, params = cpu_sample_seconds(args.steps)
-    total = sum(ts)
-    val = params * len(ts) / total / 1e6
+        reference_layer_seconds(ref, *inputs["proj"])
+    per_layer: dict[str, list[float]] = {name: [] for name, _, _ in LAYERS}
+    total, sets = 0.0, 0
+    t_start = time.perf_counter()
+    while sets < args.steps:
+        for name, _, _ in LAYERS:
+            per_layer[name].append(reference_layer_seconds(ref, *inputs[name]))
+        sets += 1
+        if time.perf_counter() - t_start > args.ref_budget:
+            break
+    total = sum(sum(v) for v in per_layer.values())
+    val = PARAMS_PER_SET * sets / total / 1e6
+    sample = (f"{sets} whole set(s) of 4 layers through the reference's own converter.rotation.rotate_weights -> "
+              f"rotate_hessian -> gptq.gptq_quantize_layer -> packing.pack_int4 on CPU tensors "
+              f"(baseline/_ref, GPTQ_DISABLE_TRITON=1), torch threads {torch.get_num_threads()}")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "Mparams/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(ts), 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "steps": sets, "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / sets, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": dict(CONFIG, parallelism="host cores"),
-        "cpu_baseline": {"value": round(val, 4), "unit": "Mparams/s", "cores": cpu_cores(), "kind": "port",
-                         "sample": "one proj layer [4096,4096] per step through oracle/cpu_ref.py (numpy + "
-                                   "LAPACK, the reference's algorithm): rotate W and H, damped Cholesky inverse, "
-                                   "GPTQ column loop, pack"},
+        "per_layer_s": {k: round(sum(v) / len(v), 3) for k, v in per_layer.items()},
+        "cpu_baseline": {"value": round(val, 4), "unit": "Mparams/s", "cores": torch.get_num_threads(),
+                         "kind": "reference", "sample": sample},
         "e2e": {"value": round(val, 4), "unit": "Mparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -270,7 +336,7 @@ def run_device(args, rank: int, world: int) -> None:
         pass
     bf16 = peaks.get("bf16_tflops", 1590.0)
     peak = bf16 / 2.0 / 3.0  # TF32 runs at half the bf16 rate; 3xTF32 issues three products
-    cpu_ts, cpu_params = cpu_sample_seconds(1)
+    cpu_ts, cpu_params, cpu_kind = cpu_sample_seconds(1)
     cpu_val = cpu_params / cpu_ts[0] / 1e6
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
@@ -292,8 +358,11 @@ def run_device(args, rank: int, world: int) -> None:
                           "ms_per_step": round(ms_max / args.steps, 3),
                           "frac": round(FLOP_PER_SET / (peak * 1e12) * 1e3 / (ms_max / args.steps), 4),
                           "note": "whole step's algorithmic flop over the 3xTF32 peak, of measured"},
-        "cpu_baseline": {"value": round(cpu_val, 4), "unit": "Mparams/s", "cores": cpu_cores(), "kind": "port",
-                         "sample": "one proj layer [4096,4096] through oracle/cpu_ref.py (numpy + LAPACK)"},
+        "cpu_baseline": {"value": round(cpu_val, 4), "unit": "Mparams/s", "cores": torch.get_num_threads(),
+                         "kind": cpu_kind,
+                         "sample": "one proj layer [4096,4096] through the reference's CPU calls (rotate_weights, "
+                                   "rotate_hessian, gptq_quantize_layer, pack_int4; baseline/_ref) or, when it "
+                                   "is not installed, oracle/cpu_ref.py"},
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -505,6 +574,8 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")
     ap.add_argument("--e2e-steps", type=int, default=12)
+    ap.add_argument("--ref-budget", type=float, default=150.0,
+                    help="reference arm: stop the timed sets after this many seconds (at least one set)")
     ap.add_argument("--streams", type=int, default=4, help="CUDA streams the layers are issued on")
     ap.add_argument("--gemm-only", type=int, default=0,
                     help="time only the dominant 3xTF32 GEMM at n^3 (small profiling case)")

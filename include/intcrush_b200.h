@@ -157,6 +157,28 @@ size_t ic_spd_inverse_workspace_size(int64_t n);
 int ic_spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Lower Cholesky factor L of an SPD matrix held as a TF32 hi/lo pair [n,n]
+ * (in place, lower triangle read), returned as its symmetric completion: the
+ * lower triangle holds L and the strictly upper triangle L^T, so that row j
+ * right of the diagonal is row j of the upper factor U = L^T.  With A = the
+ * damped inverse this is the "cholesky" Hessian method of gptq._prepare_hessian
+ * (converter/gptq.py:91-110: torch.linalg.cholesky(H^-1).T), in the layout the
+ * GPTQ column loop (ic_gptq_run) reads.  Workspace: ic_spd_inverse_workspace_size(n).
+ * Synchronises; IC_ERR_NOT_PD when a pivot is not positive (the reference then
+ * keeps the full inverse). */
+int ic_spd_cholesky(float* h_hi, float* h_lo, int64_t n, int64_t ldh, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* SmoothQuant factors of one layer (converter/smoothquant.py:11-52 and 72-102):
+ * s_j = a_j^alpha / max(max_i |W[i,j]|, 1e-8)^(1-alpha) with
+ *   mode 0: a_j = max(act[j * act_stride], 1e-8)            (per-channel activation amax)
+ *   mode 1: a_j = sqrt(max(act[j * act_stride] / nsamp, 1e-8)) (Hessian diagonal; pass the
+ *           Hessian itself with act_stride = ldh + 1)
+ * W: fp16/bf16/fp32 [M, N] (unrotated, as the pipeline's W_down.float()).  out fp32 [N].
+ * powf may differ from torch's CPU pow in the last bit. */
+int ic_smooth_factors(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, const float* act,
+                      int64_t act_stride, int mode, float alpha, float nsamp, float* out, void* stream);
+
 /* ------------------------------------------------------------------- GPTQ */
 /* Per-row scale / zero-point preparation of gptq_quantize_layer
  * (converter/gptq.py:254-317): bits 4 -> asymmetric range scales with the

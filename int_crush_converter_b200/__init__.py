@@ -28,4 +28,7 @@ from .scales import (
 from .types import QuantizationResult
 
 __version__ = "0.1.0"
-from .smoothquant import apply_smoothing_to_weight, _transform_hessian_for_smoothquant  # noqa: E402,F401
+from .smoothquant import (  # noqa: E402,F401
+    apply_smoothing_to_weight, _transform_hessian_for_smoothquant, compute_smoothing_factors,
+    compute_smoothing_from_hessian_diag,
+)

@@ -59,6 +59,8 @@ SIGNATURES = {
                               _i64, _vp, _vp, _i64, _i32, _vp]),
     "ic_spd_inverse_workspace_size": (_sz, [_i64]),
     "ic_spd_inverse": (_i32, [_vp, _vp, _i64, _i64, _f32, _vp, _sz, _vp]),
+    "ic_spd_cholesky": (_i32, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
+    "ic_smooth_factors": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i32, _f32, _f32, _vp, _vp]),
     "ic_gptq_row_params": (_i32, [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "ic_gptq_workspace_size": (_sz, [_i64, _i64, _i32, _i32]),
     "ic_gptq_run": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp,

@@ -658,6 +658,8 @@ extern "C" int ic_gptq_row_params(const float* W, int64_t M, int64_t N, int64_t 
 
 extern "C" size_t ic_gptq_workspace_size(int64_t M, int64_t N, int block_size, int superblock) {
   if (block_size <= 0) return 0;
+  if (M < 0) M = 0;  // empty shapes need no scratch (the loop returns before using any)
+  if (N < 0) N = 0;
   if (superblock < block_size) superblock = block_size;
   return loop_ws(M, N, block_size, superblock);
 }

@@ -286,6 +286,29 @@ __global__ void mirror_kernel(float* __restrict__ hi, float* __restrict__ lo, in
   }
 }
 
+// Symmetric completion of a lower triangle: H[r][c] = H[c][r] for every c > r
+// (32 x 32 tiles through shared memory; only tiles on or above the diagonal run).
+__global__ void sym_from_lower_kernel(float* __restrict__ hi, float* __restrict__ lo, int64_t n, int64_t ld) {
+  const int64_t bi = blockIdx.y, bj = blockIdx.x;
+  if (bj < bi) return;
+  __shared__ float th[32][33], tl[32][33];
+  for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
+    const int64_t r = bj * 32 + dy, c = bi * 32 + threadIdx.x;  // source tile (bj, bi)
+    if (r < n && c < n) {
+      th[dy][threadIdx.x] = hi[r * ld + c];
+      tl[dy][threadIdx.x] = lo[r * ld + c];
+    }
+  }
+  __syncthreads();
+  for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
+    const int64_t r = bi * 32 + dy, c = bj * 32 + threadIdx.x;
+    if (r < n && c < n && c > r) {
+      hi[r * ld + c] = th[threadIdx.x][dy];
+      lo[r * ld + c] = tl[threadIdx.x][dy];
+    }
+  }
+}
+
 struct Pair {
   float* hi;
   float* lo;
@@ -560,7 +583,39 @@ int spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping,
   return IC_OK;
 }
 
+int spd_cholesky(float* h_hi, float* h_lo, int64_t n, int64_t ldh, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (n <= 0) return IC_OK;
+  if (!h_hi || !h_lo) return fail(IC_ERR_INVALID, "spd_cholesky: hi/lo pair required");
+  if (ldh % 4) return fail(IC_ERR_INVALID, "spd_cholesky: ld must be a multiple of 4");
+  unsigned* flags = device_flags();
+  if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
+  Ctx c{};
+  c.H = Pair{h_hi, h_lo};
+  c.ld = ldh;
+  c.flags = flags;
+  c.st = st;
+  const size_t need = ws_layout(n, ldh, &c, ws, ws_bytes);
+  if (ws_bytes < need) return fail(IC_ERR_WORKSPACE, "spd_cholesky: workspace too small (%zu < %zu)", ws_bytes, need);
+  IC_TRY(gemm_prepare());
+  unsigned prev = 0;
+  IC_TRY(read_and_clear_flags(&prev, st));
+  IC_TRY(chol_rec(c, 0, n));
+  dim3 grid((unsigned)cdiv(n, 32), (unsigned)cdiv(n, 32));
+  sym_from_lower_kernel<<<grid, dim3(32, 8), 0, st>>>(h_hi, h_lo, n, ldh);
+  IC_CHECK_LAUNCH();
+  unsigned f = 0;
+  IC_TRY(read_and_clear_flags(&f, st));
+  if (f & DEV_TIMEOUT) return fail(IC_ERR_TIMEOUT, "spd_cholesky: a tensor-core wait timed out");
+  if (f & DEV_NOT_PD) return fail(IC_ERR_NOT_PD, "matrix is not positive definite");
+  return IC_OK;
+}
+
 }  // namespace ic
+
+extern "C" int ic_spd_cholesky(float* h_hi, float* h_lo, int64_t n, int64_t ldh, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return ic::spd_cholesky(h_hi, h_lo, n, ldh, workspace, workspace_bytes, (cudaStream_t)stream);
+}
 
 extern "C" size_t ic_spd_inverse_workspace_size(int64_t n) { return ic::spd_inverse_ws(n); }
 extern "C" int ic_spd_inverse(float* h_hi, float* h_lo, int64_t n, int64_t ldh, float damping, void* workspace,

@@ -55,6 +55,9 @@ extern "C" int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return ic::fail(IC_ERR_CUDA, "gptq_run_noalloc: no CUDA device: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return ic::fail(IC_ERR_UNSUPPORTED, "gptq_run_noalloc: device index %d", dev);
+  if (M <= 0 || N <= 0)  // nothing to do: the same argument checks and result as ic_gptq_run, no scratch
+    return ic_gptq_run(W_work, ldw, W0, ldw0, M, N, hinv_hi, hinv_lo, ldh, block_size, superblock, scale, zp,
+                       qmin, qmax, codes, ldq, packed, ldp, row_sqerr, row_maxerr, gemm_passes, nullptr, 0, stream);
   const size_t need = ic_gptq_workspace_size(M, N, block_size, superblock);
   if (need > (size_t)IC_NOALLOC_SCRATCH_BYTES)
     return ic::fail(IC_ERR_UNSUPPORTED,

@@ -117,14 +117,17 @@ def gptq_quantize_layer(W: torch.Tensor, hessian, block_size: int = 128, damping
                                    qmin, qmax, Q))
 
     def maybe_cholesky(hi, lo, n):
+        """hessian_method="cholesky" (gptq.py:91-110): the upper factor of chol(H^-1)
+        in place of H^-1, or H^-1 itself when that factorisation fails."""
         if hessian_method != "cholesky":
             return hi, lo
-        Hinv = hi[:n, :n] + lo[:n, :n]
-        L, info = torch.linalg.cholesky_ex(Hinv)  # gptq.py:91-110: upper factor of chol(H^-1)
-        if int(info.item()) != 0:
+        fh, fl = hi.clone(), lo.clone()
+        ws = workspace(lib.ic_spd_inverse_workspace_size(n), dev)
+        stc = lib.ic_spd_cholesky(fh.data_ptr(), fl.data_ptr(), n, fh.shape[1], ws.data_ptr(), ws.numel(), st)
+        if stc == nat.IC_ERR_NOT_PD:
             return hi, lo
-        from ._dev import split
-        return split(L.T.contiguous(), hi.shape[1])
+        nat.check(stc, "spd_cholesky")
+        return fh, fl
 
     if isinstance(hessian, dict):
         D = hessian["D"]

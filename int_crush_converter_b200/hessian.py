@@ -52,7 +52,8 @@ def inverse_pair(hi: torch.Tensor, lo: torch.Tensor, n: int, damping: float | No
                  H_fallback: torch.Tensor | None = None) -> str:
     """In-place (H + damping*mean(diag)*I)^-1 on a TF32 pair; returns the path taken.
 
-    SPD -> tensor-core Schur inverse ("cholesky" branch of the reference).
+    SPD -> the library's tensor-core Cholesky inverse (the reference's
+    "cholesky" branch).
     Not positive definite -> torch.linalg.inv on the GPU ("inv"), then pinv
     with the reference's warning ("pinv").  ``H_fallback`` is the undamped fp32
     matrix in the same (rotated) space, needed only for those branches; when
@@ -111,8 +112,25 @@ def dlr_to_dense(D: torch.Tensor, U: torch.Tensor) -> torch.Tensor:
     return out if D.is_cuda else out.to(D.device)
 
 
+def _abt(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """A @ B^T in 3xTF32 on the tensor cores (ic_gemm_tn), fp32 [rows(A), rows(B)]."""
+    from ._dev import split
+    ah, al = split(A)
+    bh, bl = split(B)
+    m, n, k = A.shape[0], B.shape[0], A.shape[1]
+    ld = round4(n)
+    out = torch.empty(m, ld, device=A.device, dtype=torch.float32)
+    if m and n:
+        nat.check(nat.load().ic_gemm_tn(m, n, k, 1.0, ah.data_ptr(), al.data_ptr(), ah.shape[1], bh.data_ptr(),
+                                        bl.data_ptr(), bh.shape[1], 0.0, None, None, ld, out.data_ptr(), None, ld, 3,
+                                        nat.stream_ptr(A.device)), "gemm")
+    return out[:, :n]
+
+
 def woodbury_inverse(D, U, damping: float = 0.0, device=None) -> torch.Tensor:
-    """(diag(D) + U U^T + lambda*I)^-1 by the Woodbury identity (dlr.py:75-124), on the GPU."""
+    """(diag(D) + U U^T + lambda*I)^-1 by the Woodbury identity (dlr.py:75-124), on the GPU:
+    Dinv - Z (I + U^T Z)^-1 Z^T with Z = Dinv U; the three products on the tensor
+    cores (3xTF32), the r x r inverse with the library's SPD inverse."""
     dev = device_of(D, U)
     D = f32(D, dev)
     U = f32(U, dev)
@@ -121,8 +139,12 @@ def woodbury_inverse(D, U, damping: float = 0.0, device=None) -> torch.Tensor:
         dm = (D + (U * U).sum(dim=1)).mean().clamp(min=DIAG_MEAN_FLOOR)
         D = D + damping * dm
     Dinv = 1.0 / D.clamp(min=1e-12)
-    Z = Dinv.unsqueeze(1) * U
-    Mm = torch.eye(r, device=dev) + U.T @ Z
-    Minv, _ = invert_dense(Mm, None)
-    out = torch.diag(Dinv) - Z @ Minv @ Z.T
+    Z = (Dinv.unsqueeze(1) * U).contiguous()
+    Mm = _abt(U.T.contiguous(), Z.T.contiguous())
+    Mm.diagonal().add_(1.0)
+    Minv, _ = invert_dense(Mm.contiguous(), None)
+    Y = _abt(Z, Minv.contiguous())          # Z Minv (Minv symmetric)
+    out = _abt(Y.contiguous(), Z).neg_()    # -(Z Minv) Z^T
+    out.diagonal().add_(Dinv)
+    out = out.contiguous()
     return out if device is None else out.to(device)

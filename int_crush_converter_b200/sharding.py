@@ -134,8 +134,14 @@ def reduce_row_stats(sq: torch.Tensor, mx: torch.Tensor, group=None) -> tuple[fl
     sq = sq.reshape(1).to(torch.float64).clone()
     mx = mx.reshape(1).to(torch.float32).clone()
     if world > 1:
+        # a NaN max error on any rank stays NaN, as torch's max() on one GPU does
+        # (a MAX all-reduce need not propagate NaN)
+        nan = torch.isnan(mx).to(torch.int32)
         torch.distributed.all_reduce(sq, op=torch.distributed.ReduceOp.SUM, group=group)
         torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX, group=group)
+        torch.distributed.all_reduce(nan, op=torch.distributed.ReduceOp.MAX, group=group)
+        if int(nan.item()):
+            mx.fill_(float("nan"))
     return float(sq.item()), float(mx.item())
 
 
@@ -162,6 +168,32 @@ def _quantize_rows(Wd: torch.Tensor, hi: torch.Tensor, lo: torch.Tensor, r0: int
                                      nat.ptr(zp), nat.stream_ptr(dev)), "gptq_row_params")
     rsq, rmx = _run_loop(Wl.clone(), Wl, 0, N, hi, lo, hi.shape[1], block_size, scale, zp, qmin, qmax, Q)
     return Q, scale, zp, rsq.sum(), rmx.max()
+
+
+def run_on_source(fn, src: int, group=None, device=None):
+    """Run ``fn() -> (code >= 0, payload)`` on group rank `src` and broadcast its
+    status before anything else: every rank returns (code, payload or None),
+    and if `fn` raised on the source every rank raises (the source re-raises
+    its own exception), instead of the other ranks waiting in a collective
+    that never comes."""
+    rank, world = _group_info(group)
+    if world == 1:
+        return fn()
+    err, code, payload = None, -1, None
+    if rank == src:
+        try:
+            code, payload = fn()
+        except Exception as e:  # noqa: BLE001 - re-raised below on every rank
+            err, code = e, -1
+    g_src = torch.distributed.get_global_rank(group, src) if group is not None else src
+    t = torch.tensor([code], dtype=torch.int32, device=device)
+    torch.distributed.broadcast(t, g_src, group=group)
+    c = int(t.item())
+    if c < 0:
+        if err is not None:
+            raise err
+        raise RuntimeError(f"row-sharded layer: the work of source rank {g_src} failed")
+    return c, payload
 
 
 def gptq_quantize_layer_row_sharded(W: torch.Tensor, hessian: torch.Tensor, group=None, src: int = 0,
@@ -193,21 +225,23 @@ def gptq_quantize_layer_row_sharded(W: torch.Tensor, hessian: torch.Tensor, grou
     if tuple(hessian.shape) != (N, N):
         raise ValueError(f"Hessian shape {tuple(hessian.shape)} != ({N}, {N})")
     paths = ("cholesky", "inv", "pinv")
-    if rank == src:
+
+    def invert():
         Hd = f32(hessian, dev)
         hi, lo, n = hessian_pair(Hd, 0, dev, rotate=False)
-        path = inverse_pair(hi, lo, n, damping, H_fallback=Hd)
-    else:
+        return paths.index(inverse_pair(hi, lo, n, damping, H_fallback=Hd)), (hi, lo)
+
+    code, res = run_on_source(invert, src, group, dev)
+    if res is None:
         hi = torch.empty(N, round4(N), dtype=torch.float32, device=dev)
         lo = torch.empty_like(hi)
-        path = paths[0]
+    else:
+        hi, lo = res
     if world > 1:
         g_src = torch.distributed.get_global_rank(group, src) if group is not None else src
-        code = torch.tensor([paths.index(path)], dtype=torch.int32, device=dev)
-        torch.distributed.broadcast(code, g_src, group=group)
         torch.distributed.broadcast(hi, g_src, group=group)
         torch.distributed.broadcast(lo, g_src, group=group)
-        path = paths[int(code.item())]
+    path = paths[code]
     r0, r1 = row_slice(M, rank, world)
     Q, scale, zp, sq, mx = _quantize_rows(Wd, hi, lo, r0, r1, block_size, int_bits, asymmetric)
     Q = gather_rows(Q, M, group)

@@ -118,6 +118,19 @@ def rotate_weights(W: np.ndarray, rot_size: int) -> np.ndarray:  # rotation.py:9
     return (W.reshape(M, G, rot_size) @ H.T).reshape(M, -1).astype(f32)
 
 
+def rotate_activations(x: np.ndarray, rot_size: int) -> np.ndarray:  # rotation.py:128-153
+    """Group-wise Hadamard of the last dimension (zero padded), any leading dims."""
+    x = np.asarray(x, dtype=f32)
+    if not _is_power_of_two(rot_size):
+        raise ValueError(f"rot_size must be a power of 2, got {rot_size}")
+    n = x.shape[-1]
+    if n % rot_size:
+        x = np.pad(x, [(0, 0)] * (x.ndim - 1) + [(0, rot_size - n % rot_size)])
+    lead = x.shape[:-1]
+    flat = x.reshape(-1, x.shape[-1] // rot_size, rot_size)
+    return (flat @ _hadamard(rot_size).T).reshape(*lead, -1).astype(f32)
+
+
 def rotate_hessian(H: np.ndarray, rot_size: int) -> np.ndarray:  # rotation.py:156-248
     if not _is_power_of_two(rot_size):
         raise ValueError(f"rot_size must be a power of 2, got {rot_size}")
@@ -482,9 +495,21 @@ def _result_stats(W, Q, s, zp):  # gptq.py:398-405
     return float(np.mean(d.astype(np.float64) ** 2)), float(np.abs(d).max()) if d.size else 0.0
 
 
+def prepare_hessian_cholesky(H, damping):  # gptq.py:91-110 (hessian_method="cholesky")
+    """Upper factor L^T of chol(H_damped^-1); the full inverse when that Cholesky fails."""
+    Hinv, p = invert_hessian(damp(H, damping))
+    c, info = lapack.spotrf(Hinv, lower=1, clean=1)
+    if info != 0:
+        return Hinv, p
+    return np.ascontiguousarray(c.T).astype(f32), p
+
+
 def gptq_quantize_layer(W, hessian, block_size=128, damping=0.01, int_bits=4, asymmetric=False,
-                        piso_scales=None, piso_zero_points=None):  # gptq.py:137-417 (hinv)
-    """Returns dict(quantized_W, scales(fp16), scales_f32, zero_points, mse, max_err, hinv_path)."""
+                        piso_scales=None, piso_zero_points=None, hessian_method="hinv"):  # gptq.py:137-417
+    """Returns dict(quantized_W, scales(fp16), scales_f32, zero_points, mse, max_err, hinv_path).
+
+    ``hessian_method`` "hinv" uses the damped inverse (gptq.py:113-121), "cholesky"
+    its upper Cholesky factor (gptq.py:91-110); DLR dicts always use Woodbury."""
     if int_bits not in (4, 8):
         raise ValueError(f"int_bits must be 4 or 8, got {int_bits}")
     W = np.asarray(W, dtype=f32)
@@ -499,6 +524,14 @@ def gptq_quantize_layer(W, hessian, block_size=128, damping=0.01, int_bits=4, as
     Q = np.zeros((M, N), np.int8)
     Ww = W.copy()
     paths = []
+    if hessian_method == "cholesky":
+        def prep(Hb):
+            return prepare_hessian_cholesky(Hb, damping)
+    elif hessian_method == "hinv":
+        def prep(Hb):
+            return invert_hessian(damp(Hb, damping))
+    else:
+        raise ValueError(f"hessian_method must be one of ['hinv', 'cholesky'], got '{hessian_method}'")
     if isinstance(hessian, dict):
         Hinv = woodbury_inverse(hessian["D"], hessian["U"], damping)
         gptq_block(Ww, Q, s, Hinv, 0, N, block_size, qmin, qmax, zp)
@@ -510,13 +543,13 @@ def gptq_quantize_layer(W, hessian, block_size=128, damping=0.01, int_bits=4, as
             for bi in range(nb):
                 c0 = bi * bs
                 c1 = min(c0 + bs, N)
-                Hinv, p = invert_hessian(damp(hessian[bi, :c1 - c0, :c1 - c0], damping))
+                Hinv, p = prep(hessian[bi, :c1 - c0, :c1 - c0])
                 paths.append(p)
                 gptq_block(Ww, Q, s, Hinv, c0, c1, block_size, qmin, qmax, zp)
         elif hessian.ndim == 2:
             if hessian.shape != (N, N):
                 raise ValueError(f"Hessian shape {hessian.shape} != ({N}, {N})")
-            Hinv, p = invert_hessian(damp(hessian, damping))
+            Hinv, p = prep(hessian)
             paths.append(p)
             gptq_block(Ww, Q, s, Hinv, 0, N, block_size, qmin, qmax, zp)
         else:
@@ -829,6 +862,7 @@ def apply_smoothing_to_weight(W, s):  # smoothquant.py:54-69
     return (np.asarray(W, f32) * np.asarray(s, f32)[None, :]).astype(f32)
 
 
+SMOOTHQUANT_AMAX_FLOOR = 1e-8  # config.py:148
 SMOOTHQUANT_HESSIAN_FLOOR = f32(1e-8) * f32(1e-8)  # config.py:148-152
 SANITIZE_CEIL = f32(1e30)  # config.py:78
 
@@ -840,3 +874,24 @@ def transform_hessian_for_smoothquant(H, s):  # pipeline.py:99-137 (2-D branch)
     outer = np.where(outer < SMOOTHQUANT_HESSIAN_FLOOR, SMOOTHQUANT_HESSIAN_FLOOR, outer).astype(f32)
     q = (np.asarray(H, f32) / outer).astype(f32)
     return np.where(q > SANITIZE_CEIL, SANITIZE_CEIL, q).astype(f32)
+
+
+def compute_smoothing_from_hessian_diag(hd, W, alpha=0.5, num_calibration_samples=128):  # smoothquant.py:72-102
+    """s_j = sqrt(max(H_jj / n, floor))^alpha / max(max_i |W_ij|, floor)^(1 - alpha), fp32."""
+    n = max(1, int(num_calibration_samples))
+    act = np.sqrt(_c(np.asarray(hd, f32) / f32(n), SMOOTHQUANT_AMAX_FLOOR)).astype(f32)
+    ws = _c(np.abs(np.asarray(W, f32)).max(axis=0), SMOOTHQUANT_AMAX_FLOOR).astype(f32)
+    # the power is the library call the reference makes (torch's vectorised CPU pow):
+    # numpy's pow differs from it in the last bit on a few channels
+    import torch
+    pa = torch.from_numpy(act).pow(alpha).numpy()
+    pb = torch.from_numpy(ws).pow(1.0 - alpha).numpy()
+    return (pa / pb).astype(f32)
+
+
+def compute_smoothing_factors(act_amax, W, alpha=0.5):  # smoothquant.py:11-52
+    """s_j = max(amax_j, floor)^alpha / max(max_i |W_ij|, floor)^(1 - alpha), fp32."""
+    import torch
+    act = _c(np.asarray(act_amax, f32), SMOOTHQUANT_AMAX_FLOOR).astype(f32)
+    ws = _c(np.abs(np.asarray(W, f32)).max(axis=0), SMOOTHQUANT_AMAX_FLOOR).astype(f32)
+    return (torch.from_numpy(act).pow(alpha).numpy() / torch.from_numpy(ws).pow(1.0 - alpha).numpy()).astype(f32)

@@ -156,3 +156,80 @@ def piso_inputs(case: dict):
     rng = np.random.default_rng(seed + 7)
     hd = rng.lognormal(0.0, 1.0, size=N).astype(f32) ** 2
     return W, hd.astype(f32)
+
+
+# GPTQ entry points beyond the default hinv path: the RTN fallback
+# (gptq.py:420-533), PiSO scale / zero-point overrides (gptq.py:210-252),
+# DLR Hessians through Woodbury (gptq.py:323-344, dlr.py:75-124) and
+# hessian_method="cholesky" (gptq.py:91-110)
+GPTQ_EXTRA_CASES = {
+    "gx_rtn4_sym": dict(kind="rtn", M=48, N=256, seed=101, bits=4, asym=False, ratios=None),
+    "gx_rtn4_asym_clip": dict(kind="rtn", M=48, N=256, seed=102, bits=4, asym=True, ratios=RATIOS),
+    "gx_rtn8_sym_clip": dict(kind="rtn", M=48, N=256, seed=103, bits=8, asym=False, ratios=RATIOS),
+    "gx_rtn8_asym": dict(kind="rtn", M=48, N=256, seed=104, bits=8, asym=True, ratios=None),
+    "gx_rtn4_piso": dict(kind="rtn", M=48, N=256, seed=105, bits=4, asym=False, ratios=None, piso=True),
+    "gx_rtn4_piso_zp": dict(kind="rtn", M=48, N=256, seed=106, bits=4, asym=False, ratios=None, piso=True,
+                            piso_zp=True),
+    "gx_rtn8_piso": dict(kind="rtn", M=48, N=256, seed=107, bits=8, asym=False, ratios=None, piso=True),
+    "gx_gptq4_piso": dict(kind="gptq", M=48, N=256, seed=108, bits=4, asym=False, piso=True),
+    "gx_gptq4_piso_zp": dict(kind="gptq", M=48, N=256, seed=109, bits=4, asym=False, piso=True, piso_zp=True),
+    "gx_gptq8_piso_asym": dict(kind="gptq", M=48, N=256, seed=110, bits=8, asym=True, piso=True),
+    "gx_gptq8_piso_sym": dict(kind="gptq", M=48, N=256, seed=111, bits=8, asym=False, piso=True),
+    "gx_gptq4_dlr": dict(kind="dlr", M=48, N=256, seed=112, bits=4, asym=False, rank=16),
+    "gx_gptq4_cholesky": dict(kind="cholesky", M=48, N=256, seed=113, bits=4, asym=False),
+    "gx_gptq8_cholesky_3d": dict(kind="cholesky", M=32, N=256, seed=114, bits=8, asym=False, nblk=2),
+}
+
+
+def gptq_extra_inputs(case: dict):
+    """W fp32 [M,N]; the Hessian (2-D, 3-D or DLR dict of numpy arrays, None for
+    RTN); PiSO scales [M,1] (absmax-based, jittered) and zero-points [M,1] or None."""
+    M, N, seed = case["M"], case["N"], case["seed"]
+    W = gi.weight_outlier_cols(seed, M, N)
+    rng = np.random.default_rng(seed + 5)
+    H = None
+    if case["kind"] == "dlr":
+        D = (rng.lognormal(0.0, 1.0, N) ** 2).astype(f32)
+        U = (rng.standard_normal((N, case["rank"])) * 0.5).astype(f32)
+        H = {"format": "dlr", "D": D, "U": U}
+    elif case["kind"] != "rtn":
+        H = gi.hessian_lognormal(seed + 1000, N, 2 * N)
+        if case.get("nblk"):
+            nb = case["nblk"]
+            bs = N // nb
+            H = np.stack([H[i * bs:(i + 1) * bs, i * bs:(i + 1) * bs] for i in range(nb)])
+    ps = pz = None
+    if case.get("piso"):
+        qmax = 7.0 if case["bits"] == 4 else 127.0
+        base = np.abs(W).max(axis=1, keepdims=True) / qmax
+        ps = (base * rng.uniform(0.7, 1.3, size=(M, 1))).astype(f32)
+        if case.get("piso_zp"):
+            pz = rng.integers(-3, 3, size=(M, 1)).astype(np.int8)
+    return W, H, ps, pz
+
+
+# rotation.rotate_activations (rotation.py:128-153): any leading dims, padding
+ROTACT_CASES = {
+    "ra_r64_pad_3d": dict(shape=(2, 3, 200), rot=64, seed=121),
+    "ra_r256": dict(shape=(5, 512), rot=256, seed=122),
+}
+
+
+# SmoothQuant factors from the Hessian diagonal (smoothquant.py:72-102), the
+# form config 5 (SmoothQuant alpha 0.5 with calibration Hessians) uses
+SQ_CASES = {
+    "sq_hdiag_a05": dict(M=48, N=256, seed=131, alpha=0.5, nsamp=8192),
+    "sq_hdiag_a075": dict(M=32, N=128, seed=132, alpha=0.75, nsamp=128),
+    "sq_amax_a05": dict(M=48, N=256, seed=133, alpha=0.5, nsamp=0),
+}
+
+
+def sq_inputs(case: dict):
+    W = gi.weight_outlier_cols(case["seed"], case["M"], case["N"])
+    H = gi.hessian_lognormal(case["seed"] + 1, case["N"], 2 * case["N"]) * np.float32(case["nsamp"])
+    hd = np.ascontiguousarray(np.diagonal(H)).astype(f32)
+    hd[:3] = 0.0  # dead channels hit the amax floor
+    if not case["nsamp"]:  # per-channel activation amax instead (compute_smoothing_factors)
+        hd = np.sqrt(hd).astype(f32) * f32(3.0)
+    W[:, 5] = 0.0  # an all-zero weight column hits the weight floor
+    return W, hd

@@ -154,6 +154,40 @@ def main() -> None:
         put(name, W_smooth=smoothquant.apply_smoothing_to_weight(T(W), T(s)),
             H_smooth=pipeline._transform_hessian_for_smoothquant(T(H), T(s)), chk=gi.checksum(W, H, s))
 
+
+    for name, c in C.GPTQ_EXTRA_CASES.items():
+        W, H, ps, pz = C.gptq_extra_inputs(c)
+        kw = dict(int_bits=c["bits"], asymmetric=c["asym"])
+        if ps is not None:
+            kw.update(piso_scales=T(ps), piso_zero_points=None if pz is None else T(pz))
+        if c["kind"] == "rtn":
+            r = gptq.gptq_quantize_layer_rtn(T(W), clipping_ratios=c.get("ratios"), **kw)
+        else:
+            if isinstance(H, dict):
+                Hin = {"format": "dlr", "D": T(H["D"]), "U": T(H["U"])}
+            else:
+                Hin = T(H)
+            method = "cholesky" if c["kind"] == "cholesky" else "hinv"
+            r = gptq.gptq_quantize_layer(T(W), Hin, block_size=128, damping=0.01, hessian_method=method, **kw)
+        put(name, codes=r.quantized_W, scales=r.scales, zp=r.zero_points, mse=np.float64(r.mse),
+            max_err=np.float64(r.max_err), method=np.array(r.method_used), chk=gi.checksum(W))
+        if c["kind"] == "dlr":
+            from converter import dlr
+            put(name, Hinv=dlr.woodbury_inverse(T(H["D"]), T(H["U"]), damping=0.01))
+
+    for name, c in C.ROTACT_CASES.items():
+        rng = np.random.default_rng(c["seed"])
+        x = rng.standard_normal(c["shape"]).astype(np.float32)
+        put(name, y=rotation.rotate_activations(T(x), c["rot"]))
+
+    for name, c in C.SQ_CASES.items():
+        W, hd = C.sq_inputs(c)
+        if c["nsamp"]:
+            put(name, s=smoothquant.compute_smoothing_from_hessian_diag(T(hd), T(W), alpha=c["alpha"],
+                                                                       num_calibration_samples=c["nsamp"]))
+        else:
+            put(name, s=smoothquant.compute_smoothing_factors(T(hd), T(W), alpha=c["alpha"]))
+
     np.savez_compressed(args.out, **out)
     print(f"wrote {len(out)} arrays to {args.out} ({os.path.getsize(args.out)} bytes)")
 

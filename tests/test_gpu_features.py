@@ -1,0 +1,197 @@
+"""GPU parity for the entry points beside the default GPTQ path: the RTN
+fallback, PiSO scale / zero-point overrides, DLR Hessians (Woodbury),
+hessian_method="cholesky", rotate_activations and the SmoothQuant factors,
+against golden vectors made by running the reference (tests/golden).  Also
+bounds the cost of every PiSO / greedy choice that differs from the
+reference's.
+
+Bars: RTN codes, scales and zero-points bit-exact (no rotation involved);
+GPTQ scales / zero-points bit-exact, codes >= 97% equal, and
+tr((W - deq) H (W - deq)^T) within 1% of the reference's codes for these
+small single layers (the same bar as the other single-layer GPTQ tests).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cpu_ref as R
+from tests.golden import cases as C
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    import int_crush_converter_b200 as B
+
+
+def cu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def np_(t):
+    return t.detach().cpu().numpy()
+
+
+def _dense(H):
+    if isinstance(H, dict):
+        return (np.diag(H["D"].astype(np.float64)) + H["U"].astype(np.float64) @ H["U"].T.astype(np.float64))
+    return H
+
+
+def _proxy(W, q, s, zp, H):
+    H = _dense(H)
+    if H.ndim == 3:
+        bs = H.shape[1]
+        return sum(R.proxy_loss(W[:, i * bs:(i + 1) * bs], q[:, i * bs:(i + 1) * bs], s, zp, H[i])
+                   for i in range(H.shape[0]))
+    return R.proxy_loss(W, q, s, zp, H)
+
+
+@pytest.mark.parametrize("name", list(C.GPTQ_EXTRA_CASES))
+def test_gptq_extra_entry_points(golden, name):
+    c = C.GPTQ_EXTRA_CASES[name]
+    W, H, ps, pz = C.gptq_extra_inputs(c)
+    kw = dict(int_bits=c["bits"], asymmetric=c["asym"])
+    if ps is not None:
+        kw.update(piso_scales=cu(ps), piso_zero_points=None if pz is None else cu(pz))
+    if c["kind"] == "rtn":
+        r = B.gptq_quantize_layer_rtn(cu(W), clipping_ratios=c.get("ratios"), **kw)
+    else:
+        Hin = {"format": "dlr", "D": cu(H["D"]), "U": cu(H["U"])} if isinstance(H, dict) else cu(H)
+        method = "cholesky" if c["kind"] == "cholesky" else "hinv"
+        r = B.gptq_quantize_layer(cu(W), Hin, block_size=128, damping=0.01, hessian_method=method, **kw)
+    gq, gs = golden[name + "/codes"], golden[name + "/scales"]
+    gz = golden[name + "/zp"] if name + "/zp" in golden.files else None
+    assert np.array_equal(np_(r.scales), gs)
+    assert (r.zero_points is None) == (gz is None)
+    if gz is not None:
+        assert np.array_equal(np_(r.zero_points), gz)
+    q = np_(r.quantized_W)
+    if c["kind"] == "rtn":
+        assert np.array_equal(q, gq)
+        assert r.method_used == ("rtn_piso_b200" if c.get("piso") else "rtn_b200")
+        assert abs(r.mse / float(golden[name + "/mse"]) - 1) < 1e-6
+        return
+    assert np.mean(q == gq) >= 0.97
+    s32 = gs.astype(np.float32)
+    p = _proxy(W, q, s32, gz, H)
+    p_ref = _proxy(W, gq, s32, gz, H)
+    assert abs(p / p_ref - 1) < 0.01, (p, p_ref)
+    assert abs(r.mse / float(golden[name + "/mse"]) - 1) < 0.01
+
+
+def test_woodbury_inverse_matches_reference(golden):
+    name = "gx_gptq4_dlr"
+    _, H, _, _ = C.gptq_extra_inputs(C.GPTQ_EXTRA_CASES[name])
+    g = golden[name + "/Hinv"]
+    out = np_(B.woodbury_inverse(cu(H["D"]), cu(H["U"]), damping=0.01))
+    np.testing.assert_allclose(out, g, rtol=0, atol=1e-5 * np.abs(g).max())
+
+
+def test_cholesky_factor_of_inverse():
+    """The library's Cholesky (ic_spd_cholesky) against LAPACK's on a damped
+    inverse: lower triangle L, strictly upper triangle L^T."""
+    from int_crush_converter_b200 import _native as nat
+    from int_crush_converter_b200._dev import split
+    from tests.golden import inputs as gi
+    n = 384
+    Hd = R.damp(gi.hessian_lognormal(5, n, 1024), 0.01)
+    Hinv, _ = R.invert_hessian(Hd)
+    L = np.linalg.cholesky(Hinv.astype(np.float64))
+    hi, lo = split(cu(Hinv))
+    lib = nat.load()
+    ws = torch.empty(lib.ic_spd_inverse_workspace_size(n), dtype=torch.uint8, device="cuda")
+    nat.check(lib.ic_spd_cholesky(hi.data_ptr(), lo.data_ptr(), n, hi.shape[1], ws.data_ptr(), ws.numel(),
+                                  nat.stream_ptr(hi.device)))
+    got = np_(hi[:, :n] + lo[:, :n]).astype(np.float64)
+    sym = np.tril(L) + np.triu(L.T, 1)
+    assert np.abs(got - sym).max() <= 1e-5 * np.abs(L).max()
+    bad = cu(-np.eye(8, dtype=np.float32))
+    bh, bl = split(bad)
+    st = lib.ic_spd_cholesky(bh.data_ptr(), bl.data_ptr(), 8, bh.shape[1], ws.data_ptr(), ws.numel(),
+                             nat.stream_ptr(bh.device))
+    assert st == nat.IC_ERR_NOT_PD
+
+
+@pytest.mark.parametrize("name", list(C.ROTACT_CASES))
+def test_rotate_activations(golden, name):
+    c = C.ROTACT_CASES[name]
+    x = np.random.default_rng(c["seed"]).standard_normal(c["shape"]).astype(np.float32)
+    g = golden[name + "/y"]
+    y = np_(B.rotate_activations(cu(x), c["rot"]))
+    assert y.shape == g.shape
+    np.testing.assert_allclose(y, g, rtol=0, atol=2e-6 * np.abs(g).max())
+    yh = B.rotate_activations(cu(x).half(), c["rot"])
+    assert yh.dtype == torch.float16 and tuple(yh.shape) == g.shape
+
+
+@pytest.mark.parametrize("name", list(C.SQ_CASES))
+def test_smoothing_factors(golden, name):
+    """powf against torch's CPU pow: at most 4 fp32 ulp apart (measured: 0-2)."""
+    c = C.SQ_CASES[name]
+    W, hd = C.sq_inputs(c)
+    if c["nsamp"]:
+        s = B.compute_smoothing_from_hessian_diag(cu(hd), cu(W).half(), alpha=c["alpha"],
+                                                  num_calibration_samples=c["nsamp"])
+    else:
+        s = B.compute_smoothing_factors(cu(hd), cu(W).half(), alpha=c["alpha"])
+    g = golden[name + "/s"]
+    ulp = np.abs(np_(s).view(np.int32).astype(np.int64) - g.view(np.int32).astype(np.int64))
+    assert ulp.max() <= 4, ulp.max()
+
+
+def _piso_cost(W, h, s, zp, qmin, qmax):
+    """sum_d h_d (w_d - deq_d)^2 per row (fp64) for the candidate (s, zp) (piso.py:29-182)."""
+    W = W.astype(np.float32)
+    s = s.reshape(-1, 1).astype(np.float32)
+    if zp is None:
+        q = np.clip(R.rhaz(W / s), qmin, qmax)
+        deq = q.astype(np.float64) * s
+    else:
+        z = zp.reshape(-1, 1).astype(np.float32)
+        q = np.clip(R.rhaz(W / s + z), qmin, qmax)
+        deq = (q.astype(np.float64) - z) * s
+    return ((W - deq) ** 2 * h.astype(np.float64)).sum(axis=1)
+
+
+@pytest.mark.parametrize("name", list(C.PISO_CASES))
+def test_piso_choices_cost_bound(golden, name):
+    """>= 95% of rows pick the reference's candidate exactly, and every row's
+    choice costs at most 5e-5 more (relative) than the reference's: candidates
+    whose fp32 costs (512 terms, rounding ~512 * 2^-24) tie are interchangeable."""
+    c = C.PISO_CASES[name]
+    W, hd = C.piso_inputs(c)
+    f = dict(int8=B.compute_piso_scales_int8, int4=B.compute_piso_scales_int4,
+             int8_asym=B.compute_piso_scales_int8_asymmetric,
+             int4_asym=B.compute_piso_scales_int4_asymmetric)[c["kind"]]
+    qm = (-8, 7) if "int4" in c["kind"] else (-128, 127)
+    o = f(cu(W), cu(hd))
+    if isinstance(o, tuple):
+        s, zp = np_(o[0]), np_(o[1])
+        gz = golden[name + "/zp"]
+    else:
+        s, zp, gz = np_(o), None, None
+    gs = golden[name + "/scales"]
+    assert np.mean(s == gs) >= 0.95
+    mine = _piso_cost(W, hd, s, zp, *qm)
+    ref = _piso_cost(W, hd, gs, gz, *qm)
+    assert np.all(mine <= ref * (1 + 5e-5) + 1e-30), np.max(mine / ref - 1)
+
+
+@pytest.mark.parametrize("name", list(C.GREEDY_CASES))
+def test_greedy_rows_cost_bound(golden, name):
+    """Per row, e H e^T of the greedy result within 1e-3 (relative) of the
+    reference's: coordinate descent rows are independent, and rows whose codes
+    differ took a tie broken differently by fp32 rounding."""
+    c = C.GREEDY_CASES[name]
+    W, Q, S, H = C.greedy_inputs(c)
+    qm = (-8, 7) if c["bits"] == 4 else (-128, 127)
+    out = np_(B.greedy_local_search(cu(W), cu(Q), cu(S), cu(H), c["passes"], *qm))
+    g = golden[name + "/codes"]
+    Hd = H.astype(np.float64)
+
+    def rowcost(q):
+        E = q.astype(np.float64) * S - W
+        return np.einsum("ij,ij->i", E @ Hd, E)
+    assert np.all(rowcost(out) <= rowcost(g) * (1 + 1e-3) + 1e-30)
+    assert np.mean(out == g) > 0.99

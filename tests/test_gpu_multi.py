@@ -35,7 +35,10 @@ def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    import datetime
+    # a lost peer ends the next collective with an error instead of a hang
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                         timeout=datetime.timedelta(seconds=60))
     try:
         import int_crush_converter_b200 as B
         from int_crush_converter_b200 import sharding as S
@@ -57,9 +60,16 @@ def test_row_sharded_layer_on_two_gpus():
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in range(world)]
+    try:
+        res = [q.get(timeout=300) for _ in range(world)]
+    finally:
+        # a worker that died leaves its peer in a collective: end both
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     for p in procs:
-        p.join(timeout=120)
         assert p.exitcode == 0
     for r in res:
         assert all(r[1:6]), r

@@ -143,3 +143,45 @@ def test_smoothing_matches_reference(golden, name):
     W, H, s = C.smooth_inputs(C.SMOOTH_CASES[name])
     assert np.array_equal(R.apply_smoothing_to_weight(W, s), golden[name + "/W_smooth"])
     assert np.array_equal(R.transform_hessian_for_smoothquant(H, s), golden[name + "/H_smooth"])
+
+
+@pytest.mark.parametrize("name", list(C.GPTQ_EXTRA_CASES))
+def test_gptq_extra_entry_points(golden, name):
+    """RTN fallback, PiSO overrides, DLR (Woodbury) and hessian_method='cholesky'."""
+    c = C.GPTQ_EXTRA_CASES[name]
+    W, H, ps, pz = C.gptq_extra_inputs(c)
+    assert gi.checksum(W) == str(golden[name + "/chk"])
+    if c["kind"] == "rtn":
+        r = R.gptq_quantize_layer_rtn(W, c["bits"], c["asym"], c.get("ratios"), ps, pz)
+    else:
+        method = "cholesky" if c["kind"] == "cholesky" else "hinv"
+        r = R.gptq_quantize_layer(W, H, 128, 0.01, c["bits"], c["asym"], ps, pz, hessian_method=method)
+    assert np.array_equal(r["quantized_W"], golden[name + "/codes"])
+    assert np.array_equal(r["scales"], golden[name + "/scales"])
+    if r["zero_points"] is None:
+        assert name + "/zp" not in golden.files
+    else:
+        assert np.array_equal(r["zero_points"], golden[name + "/zp"])
+    assert abs(r["mse"] / float(golden[name + "/mse"]) - 1) < 1e-6
+    if c["kind"] == "dlr":
+        g = golden[name + "/Hinv"]
+        np.testing.assert_allclose(R.woodbury_inverse(H["D"], H["U"], 0.01), g, rtol=0, atol=1e-5 * np.abs(g).max())
+
+
+@pytest.mark.parametrize("name", list(C.ROTACT_CASES))
+def test_rotate_activations(golden, name):
+    c = C.ROTACT_CASES[name]
+    x = np.random.default_rng(c["seed"]).standard_normal(c["shape"]).astype(np.float32)
+    g = golden[name + "/y"]
+    np.testing.assert_allclose(R.rotate_activations(x, c["rot"]), g, rtol=0, atol=2e-6 * np.abs(g).max())
+
+
+@pytest.mark.parametrize("name", list(C.SQ_CASES))
+def test_smoothing_factors_from_hessian_diag(golden, name):
+    c = C.SQ_CASES[name]
+    W, hd = C.sq_inputs(c)
+    if c["nsamp"]:
+        s = R.compute_smoothing_from_hessian_diag(hd, W, c["alpha"], c["nsamp"])
+    else:
+        s = R.compute_smoothing_factors(hd, W, c["alpha"])
+    assert np.array_equal(s, golden[name + "/s"])

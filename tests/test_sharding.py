@@ -136,3 +136,54 @@ def test_row_sharded_validates_without_a_gpu():
         S.gptq_quantize_layer_row_sharded(W, torch.eye(8), int_bits=3)
     with pytest.raises(ValueError):
         S.gptq_quantize_layer_row_sharded(W, torch.eye(8), src=1)
+
+
+def _fail_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=60))
+    out = []
+    try:
+        # a source rank that raises: every rank raises, none waits
+        def boom():
+            raise ValueError("inverse failed here")
+        try:
+            S.run_on_source(boom, 0, device="cpu")
+            out.append("no error")
+        except ValueError as e:
+            out.append(("ValueError", str(e)))
+        except RuntimeError as e:
+            out.append(("RuntimeError", str(e)))
+        # a source rank that succeeds: every rank gets its code
+        out.append(S.run_on_source(lambda: (2, "payload"), 1, device="cpu")[0])
+        # a NaN max error on one rank stays NaN after the reduction
+        sq, mx = S.reduce_row_stats(torch.tensor(1.0, dtype=torch.float64),
+                                    torch.tensor(float("nan") if rank == 1 else 3.0))
+        out.append((sq, mx != mx))
+        q.put((rank, out))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_two_gloo_ranks_source_failure_and_nan_stats():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fail_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[0][0] == ("ValueError", "inverse failed here")
+    assert res[1][0][0] == "RuntimeError"
+    for r in (0, 1):
+        assert res[r][1] == 2
+        assert res[r][2] == (2.0, True)
+    assert all(p.exitcode == 0 for p in procs)

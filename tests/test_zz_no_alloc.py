@@ -54,7 +54,9 @@ def _run(fn_name, W, hi, lo, bs, sb, ws=None):
 def test_noalloc_matches_workspace_entry_twice():
     from int_crush_converter_b200 import _native as nat
     lib = nat.load()
-    for (M, N, bs, sb, seed) in [(512, 1024, 128, 512, 3), (300, 640, 64, 256, 4)]:
+    # the last case has a block size that is not a multiple of 4, which carves
+    # the staging slices of the far update from the array as well
+    for (M, N, bs, sb, seed) in [(512, 1024, 128, 512, 3), (300, 640, 64, 256, 4), (300, 640, 6, 6, 5)]:
         W, hi, lo = _inputs(M, N, seed)
         ws = torch.empty(lib.ic_gptq_workspace_size(M, N, bs, sb), dtype=torch.uint8, device="cuda")
         ref = _run("ic_gptq_run", W, hi, lo, bs, sb, ws)
@@ -73,3 +75,12 @@ def test_noalloc_rejects_oversized_shape():
                                      None, N, None, 0, None, None, 3, nat.stream_ptr(torch.device("cuda")))
     assert status == nat.IC_ERR_UNSUPPORTED
     assert "scratch" in nat.last_error()
+    # empty and negative shapes: nothing to do, the same answer as the workspace entry point
+    for m, n in [(0, N), (-3, N), (4, -1)]:
+        args = [None, N, None, N, m, n, None, None, N, 128, 1024, None, None, -8, 7, None, N, None, 0, None,
+                None, 3]
+        scale = torch.empty(4, device="cuda")
+        args[11] = scale.data_ptr()
+        a = lib.ic_gptq_run_noalloc(*args, nat.stream_ptr(torch.device("cuda")))
+        b = lib.ic_gptq_run(*args, None, 0, nat.stream_ptr(torch.device("cuda")))
+        assert a == b == nat.IC_OK
