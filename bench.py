@@ -1,23 +1,32 @@
-"""Benchmark: GPTQ-INT4 rot-256 Mparams quantized/s (BASELINE.json metric, config 3).
+"""Benchmark: GPTQ-INT4 rot-256 Mparams quantized/s (BASELINE.json metric) on a
+fixed model at 1/2/4/8 B200 (config 5's workload; strong scaling).
 
-A "step" quantizes one synthetic DiT linear set -- qkv [12288,4096],
-proj [4096,4096], mlp_up [16384,4096], mlp_down [4096,16384] (201.3 M params)
--- through the whole per-layer hot path: rotate W (fp16 in HBM) and its
-Hessian, row scales / zero-points, damping, tensor-core inverse, GPTQ column
-loop with the lazy tensor-core update, INT4 packing and the verify statistics.
-Each layer's Hessian is H = X^T X / 8192 with X rows N(0, diag(s^2)),
-s ~ LogNormal(0, 1) (seeded, generated on the device before timing).  Sets are
-resident in HBM (~1.7 GB each, far larger than L2) and cycled, so no step
-reads a warm input.
+The workload is the synthetic 9B-parameter DiT of config 5: 40 linear sets (8
+double-stream blocks x {img, txt} + 24 single-stream blocks) of qkv
+[12288,4096], proj [4096,4096], mlp_up [16384,4096] and mlp_down [4096,16384],
+8.05e9 parameters, GPTQ INT4 rot256, block 128, damping 0.01, SmoothQuant
+alpha 0.5 (which with rotation is SmoothRot on the FFN down layers: factors
+from the per-channel activation amax, W * s and H / (s_i s_j) fused into the
+rotations, the Hessian in the pipeline's own rotate-smooth-rotate order) and
+PermuQuant tau 0.  One step quantizes the whole model: every layer through the
+whole per-layer path (rotate W and H, row scales / zero-points, damping,
+tensor-core inverse, GPTQ column loop with the tensor-core lazy update, INT4
+packing, verify statistics), the layers handed out by a work queue across the
+ranks (longest first), and every layer's packed codes, scales, zero-points and
+statistics gathered to rank 0 over NVLink.  Inputs are seeded synthetic
+tensors resident in HBM (a pool of distinct sets per rank, each ~1.7 GB, far
+larger than L2, cycled over the model's 40 sets).
+
+PermuQuant at INT4 uses per-row groups (pipeline.py:604): a column permutation
+leaves every row's absmax, scale and codes unchanged, so its acceptance test
+(relative improvement > tau = 0, permuquant.py:143-149) is false in exact
+arithmetic and no permutation is applied; the reference decides it on the
+summation-order noise of two fp32 sums.
 
 Modes:
   python bench.py [--gpus N --steps K --warmup W]      B200 path (one process per GPU)
-  python bench.py --impl reference ...                 the reference's CPU algorithm (oracle
-                                                       restatement) on the host cores
-Layers are issued on four CUDA streams (LayerStreams), so consecutive steps
-overlap; the default 24 steps measure that steady state.
-Multi-GPU: each rank quantizes its own sets (layers are independent, weak
-scaling); timing is the max over ranks of the device-event time.
+  python bench.py --impl reference ...                 the reference's own CPU code (baseline/_ref)
+  python bench.py --hbm-kernels | --configs | --gemm-only N | --one-step
 """
 
 from __future__ import annotations
@@ -47,16 +56,22 @@ BLOCK_COLS = 128
 FLOP_PER_SET = sum(2 * m * n * (n - BLOCK_COLS) + n ** 3 for _, m, n in LAYERS)
 N_SAMPLES = 8192
 ROT, BLOCK, DAMP = 256, 128, 0.01
+SMOOTH_ALPHA = 0.5
+MODEL_SETS = 40  # 8 double-stream blocks x (img, txt) + 24 single-stream blocks
 METRIC = "GPTQ-INT4 rot256 Mparams quantized/s"
-CONFIG = {"workload": "config 3: GPTQ INT4 rot256, block 128, damping 0.01; one step = one synthetic DiT linear "
-                      "set qkv[12288,4096] proj[4096,4096] mlp_up[16384,4096] mlp_down[4096,16384] (201.3M params), "
+CONFIG = {"workload": "config 5: synthetic 9B DiT, 40 linear sets of qkv[12288,4096] proj[4096,4096] "
+                      "mlp_up[16384,4096] mlp_down[4096,16384] (8.05e9 params); GPTQ INT4 rot256, block 128, "
+                      "damping 0.01; SmoothQuant alpha 0.5 -> SmoothRot on the 40 mlp_down layers; PermuQuant tau 0 "
+                      "(INT4 per-row groups: never accepted in exact arithmetic, no permutation); one step = the "
+                      "whole model, layers from a work queue over the ranks, outputs gathered to rank 0; "
                       "fp16 W ~ N(0,0.02^2), H = X^T X/8192 with X rows N(0, diag(s^2)), s ~ LogNormal(0,1)",
-          "rot_size": ROT, "block_size": BLOCK, "damping": DAMP, "int_bits": 4,
-          "l2": "inputs larger than L2 (each set ~1.7 GB, sets cycled)"}
+          "rot_size": ROT, "block_size": BLOCK, "damping": DAMP, "int_bits": 4, "smooth_alpha": SMOOTH_ALPHA,
+          "l2": "inputs larger than L2 (each set ~1.7 GB, a pool of sets cycled over the model)"}
 
 
 def make_set(seed: int, dev: torch.device):
-    """One synthetic linear set on the device: fp16 W ~ N(0, 0.02^2), H = X^T X / 8192."""
+    """One synthetic linear set on the device: (name, fp16 W ~ N(0, 0.02^2), H = X^T X / 8192,
+    per-channel activation amax max_t |X[t, j]|) per layer."""
     g = torch.Generator(device=dev).manual_seed(seed)
     out = []
     prev = torch.backends.cuda.matmul.allow_tf32
@@ -65,13 +80,15 @@ def make_set(seed: int, dev: torch.device):
         W = (torch.randn(m, n, generator=g, device=dev) * 0.02).half()
         s = torch.exp(torch.randn(n, generator=g, device=dev))  # LogNormal(0, 1) channel scales
         H = torch.zeros(n, n, device=dev)
+        amax = torch.zeros(n, device=dev)
         for c0 in range(0, N_SAMPLES, 2048):  # X in chunks to bound the temporary
             X = torch.randn(min(2048, N_SAMPLES - c0), n, generator=g, device=dev) * s
             H.addmm_(X.T, X)
+            amax = torch.maximum(amax, X.abs().amax(dim=0))
             del X
         H.div_(N_SAMPLES)
         H = 0.5 * (H + H.T)
-        out.append((name, W, H))
+        out.append((name, W, H, amax))
     torch.backends.cuda.matmul.allow_tf32 = prev
     return out
 
@@ -136,10 +153,8 @@ REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
 def _reference_converter():
-    """The unmodified reference package installed under baseline/_ref (pip --target),
-    with its Triton path switched off through its own switch (gptq.py:24) so that
-    it runs its CPU PyTorch code; None when it is not installed."""
-    os.environ["GPTQ_DISABLE_TRITON"] = "1"
+    """The unmodified reference package installed under baseline/_ref (pip --target);
+    None when it is not installed."""
     if not os.path.isdir(os.path.join(REF_DIR, "converter")):
         return None
     if REF_DIR not in sys.path:
@@ -174,26 +189,18 @@ def reference_layer_seconds(ref, W, H) -> float:
     return time.perf_counter() - t0
 
 
-def cpu_sample_seconds(reps: int = 1):
-    """The reference's CPU path on the proj layer [4096, 4096] of a seeded set
-    (baseline/_ref when installed, else the oracle restatement); returns
-    (seconds per rep, params, kind)."""
-    name, m, n = LAYERS[1]
-    ref = _reference_converter()
-    if ref is not None:
-        W, H = cpu_layer_inputs(name, m, n, 4321)
-        return [reference_layer_seconds(ref, W, H) for _ in range(reps)], m * n, "reference"
-    from oracle import cpu_ref as R
-    from tests.golden import inputs as gi
-    W = gi.weight_outlier_cols(1234, m, n, frac=0.0005, mult=1.0)
-    H = gi.hessian_lognormal(4321, n, N_SAMPLES)
-    ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        r = R.gptq_quantize_layer(R.rotate_weights(W, ROT), R.rotate_hessian(H, ROT), BLOCK, DAMP, 4)
-        R.pack_int4(r["quantized_W"])
-        ts.append(time.perf_counter() - t0)
-    return ts, m * n, "port"
+def reference_cpu_subprocess(steps: int, warmup: int, budget: float, sample: str = "set") -> dict | None:
+    """Run the reference's CPU arm in a child process that sees no GPU; its JSON line or None."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE"):
+        env.pop(k, None)
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference-cpu", "--steps", str(steps),
+           "--warmup", str(warmup), "--ref-budget", str(budget), "--ref-sample", sample]
+    p = subprocess.run(cmd, env=env, stdout=subprocess.PIPE, text=True)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    if p.returncode != 0 or not lines:
+        return None
+    return json.loads(lines[-1])
 
 
 def cpu_cores() -> int:
@@ -204,38 +211,69 @@ def cpu_cores() -> int:
 
 
 def run_reference(args, rank: int, world: int) -> None:
-    """The reference's own CPU implementation on the B200 arm's config: one step =
-    one DiT linear set (qkv, proj, mlp_up, mlp_down) through its per-layer calls,
-    all host threads.  A set takes about a minute of CPU, so the timed steps stop
-    at --ref-budget seconds (after at least one whole set); `steps` reports the
-    sets actually timed.  Warm-up steps run the proj layer only."""
+    """The reference arm: its own CPU implementation timed in a child process
+    that sees no GPU (the reference picks its Triton GPU loop whenever CUDA is
+    visible, gptq.py:61-62, and has no switch for it), plus, as context, one set
+    through its stock path on this box (Triton GPTQ loop on the GPU, rotations
+    and inverse on the CPU).  Rank 0 only."""
     if rank != 0:
         return
+    line = reference_cpu_subprocess(args.steps, args.warmup, args.ref_budget)
+    if line is None:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's CPU run failed"}), flush=True)
+        return
+    if "unavailable" not in line:
+        line["n_gpus"] = world
+        ref = _reference_converter()
+        if ref is not None and torch.cuda.is_available():
+            tot = 0.0
+            for i, (name, m, n) in enumerate(LAYERS):
+                tot += reference_layer_seconds(ref, *cpu_layer_inputs(name, m, n, 77 + i))
+            line["stock_path_one_set"] = {
+                "value": round(PARAMS_PER_SET / tot / 1e6, 4), "unit": "Mparams/s", "seconds": round(tot, 3),
+                "note": "the reference's default code path on this box: Triton GPTQ loop on the GPU "
+                        "(gptq.py:27-88), rotations and the Hessian inverse on the CPU"}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_cpu(args) -> None:
+    """The reference's own CPU implementation on the B200 arm's config: one step =
+    one DiT linear set (qkv, proj, mlp_up, mlp_down) through its per-layer calls,
+    all host threads.  A set takes tens of seconds of CPU, so the timed steps stop
+    at --ref-budget seconds (after at least one whole set); `steps` reports the
+    sets actually timed.  Warm-up steps run the proj layer only.  Run with no GPU
+    visible."""
+    if torch.cuda.is_available():
+        raise RuntimeError("the reference's CPU arm must run with no GPU visible (CUDA_VISIBLE_DEVICES=)")
     ref = _reference_converter()
     if ref is None:
         print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref "
                                                                "(pip install --target baseline/_ref)"}), flush=True)
         return
     torch.set_num_threads(cpu_cores())
-    inputs = {name: cpu_layer_inputs(name, m, n, 77 + i) for i, (name, m, n) in enumerate(LAYERS)}
+    inputs = {name: cpu_layer_inputs(name, m, n, 77 + i) for i, (name, m, n) in enumerate(LAYERS)
+              if args.ref_sample == "set" or name == "proj"}
     for _ in range(args.warmup):
         reference_layer_seconds(ref, *inputs["proj"])
-    per_layer: dict[str, list[float]] = {name: [] for name, _, _ in LAYERS}
+    layers = LAYERS if args.ref_sample == "set" else [LAYERS[1]]
+    per_step_params = sum(m * n for _, m, n in layers)
+    per_layer: dict[str, list[float]] = {name: [] for name, _, _ in layers}
     total, sets = 0.0, 0
     t_start = time.perf_counter()
     while sets < args.steps:
-        for name, _, _ in LAYERS:
+        for name, _, _ in layers:
             per_layer[name].append(reference_layer_seconds(ref, *inputs[name]))
         sets += 1
         if time.perf_counter() - t_start > args.ref_budget:
             break
     total = sum(sum(v) for v in per_layer.values())
-    val = PARAMS_PER_SET * sets / total / 1e6
-    sample = (f"{sets} whole set(s) of 4 layers through the reference's own converter.rotation.rotate_weights -> "
+    val = per_step_params * sets / total / 1e6
+    what = "whole set(s) of 4 layers" if args.ref_sample == "set" else "proj layer(s) [4096,4096]"
+    sample = (f"{sets} {what} through the reference's own converter.rotation.rotate_weights -> "
               f"rotate_hessian -> gptq.gptq_quantize_layer -> packing.pack_int4 on CPU tensors "
-              f"(baseline/_ref, GPTQ_DISABLE_TRITON=1), torch threads {torch.get_num_threads()}")
+              f"(baseline/_ref, no GPU visible), torch threads {torch.get_num_threads()}")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "Mparams/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "Mparams/s", "n_gpus": 0,
         "steps": sets, "steps_requested": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * total / sets, 2),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -250,21 +288,23 @@ def run_reference(args, rank: int, world: int) -> None:
 
 # ----------------------------------------------------------------------------- B200 arm
 def dominant_gemm_tflops(dev: torch.device, n: int = 16384, reps: int = 3) -> tuple[float, float]:
-    """The dominant kernel (3xTF32 tcgen05 GEMM) at the largest shape a step runs
-    (the n x n x n product H^-1 = U U^T of the mlp_down inverse), timed with CUDA
-    events on the launching stream.  Returns (algorithmic TFLOP/s, ms per launch)."""
+    """The dominant kernel (3xTF32 tcgen05 GEMM) at the largest product a step
+    runs: H^-1 = U U^T of the mlp_down inverse, U upper triangular [16384,16384],
+    lower output tiles only (ic_gemm_tn_tri, tri = 3), exactly as the inverse
+    issues it; timed with CUDA events on the launching stream.  Algorithmic flop
+    n^3 / 3 (the triangular product).  Returns (TFLOP/s, ms per launch)."""
     from int_crush_converter_b200 import _native as nat
     lib = nat.load()
     g = torch.Generator(device=dev).manual_seed(7)
-    hi = torch.randn(n, n, generator=g, device=dev)
-    lo = torch.zeros_like(hi)
+    hi = torch.randn(n, n, generator=g, device=dev).triu_()
+    lo = (torch.randn(n, n, generator=g, device=dev) * 1e-4).triu_()
     out_hi = torch.empty_like(hi)
     out_lo = torch.empty_like(hi)
     st = nat.stream_ptr(dev)
 
     def go():
-        nat.check(lib.ic_gemm_tn(n, n, n, 1.0, hi.data_ptr(), lo.data_ptr(), n, hi.data_ptr(), lo.data_ptr(), n,
-                                 0.0, None, None, n, out_hi.data_ptr(), out_lo.data_ptr(), n, 3, st), "gemm")
+        nat.check(lib.ic_gemm_tn_tri(n, n, n, 1.0, hi.data_ptr(), lo.data_ptr(), n, hi.data_ptr(), lo.data_ptr(), n,
+                                     0.0, None, None, n, out_hi.data_ptr(), out_lo.data_ptr(), n, 3, st), "gemm")
     go()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -275,7 +315,51 @@ def dominant_gemm_tflops(dev: torch.device, n: int = 16384, reps: int = 3) -> tu
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / reps
     del hi, lo, out_hi, out_lo
-    return 2.0 * n ** 3 / (ms * 1e-3) / 1e12, ms
+    return n ** 3 / 3.0 / (ms * 1e-3) / 1e12, ms
+
+
+def model_layers(n_sets: int) -> list[tuple[int, str, int, int]]:
+    """(set, layer name, out, in) of every linear layer of the model."""
+    return [(si, name, m, n) for si in range(n_sets) for name, m, n in LAYERS]
+
+
+def layer_order(layers, how: str) -> list[int]:
+    from int_crush_converter_b200.sharding import layer_cost, longest_first
+    if how == "natural":
+        return list(range(len(layers)))
+    return longest_first([layer_cost(m, n) for _, _, m, n in layers])
+
+
+def output_specs(layers):
+    def specs(i):
+        m, n = layers[i][2], layers[i][3]
+        return {"packed": ((m, n // 2), torch.uint8), "scales": ((m, 1), torch.float16),
+                "zero_points": ((m, 1), torch.int8), "stats": ((3,), torch.float64)}
+    return specs
+
+
+def smoothrot_hook(amax: torch.Tensor):
+    """SmoothRot pre-pass of an FFN down layer (pipeline.py:362-415): factors from
+    the activation amax and the unrotated weight, on the device."""
+    from int_crush_converter_b200.smoothquant import compute_smoothing_factors
+
+    def before(Wd):
+        a = amax if amax.is_cuda else amax.to(Wd.device, non_blocking=True)
+        return {"smoothing": compute_smoothing_factors(a, Wd, alpha=SMOOTH_ALPHA), "smoothing_order": "pipeline"}
+    return before
+
+
+def run_model_steps(args, tag, steps, layers, order, fetch, pool, world, dev, on_gathered=None):
+    """`steps` whole-model steps: work queue -> quantize -> gather to rank 0."""
+    from int_crush_converter_b200.sharding import WorkQueue, gather_results, quantize_from_queue
+    specs = output_specs(layers)
+    for k in range(steps):
+        res = quantize_from_queue(WorkQueue(order, f"{tag}{k}"), fetch, pool, depth=args.depth)
+        pool.join()
+        if world > 1:
+            res = gather_results(res, len(layers), specs, dst=0, device=dev)
+        if on_gathered is not None:
+            on_gathered(res)
 
 
 def run_device(args, rank: int, world: int) -> None:
@@ -286,23 +370,35 @@ def run_device(args, rank: int, world: int) -> None:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     nat.require_device(dev)
-    n_sets = max(1, min(args.sets, args.steps))
-    sets = [make_set(1000 * rank + i, dev) for i in range(n_sets)]
+    layers = model_layers(args.model_sets)
+    order = layer_order(layers, args.order)
+    n_params = sum(m * n for _, _, m, n in layers)
+    n_flop = args.model_sets * FLOP_PER_SET
+    n_pool = max(1, min(args.sets, args.model_sets))
+    sets = [{name: (W, H, a) for name, W, H, a in make_set(1000 * rank + i, dev)} for i in range(n_pool)]
     pool = B.LayerStreams(args.streams, dev)
 
-    def step(i):
-        for name, W, H in sets[i % n_sets]:
-            pool.submit(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP)
+    def fetch(i):
+        si, name, _, _ = layers[i]
+        W, H, amax = sets[si % n_pool][name]
+        kw = dict(rot_size=ROT, block_size=BLOCK, damping=DAMP)
+        if name == "mlp_down":
+            kw["before"] = smoothrot_hook(amax)
+        return W, H, kw
 
-    with pool:
-        for i in range(args.warmup):
-            step(i)
+    pool.fork()
+    run_model_steps(args, "w", args.warmup, layers, order, fetch, pool, world, dev)
+    pool.check()
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     lib = nat.load()
     cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     phys = int(cvd.split(",")[local]) if cvd and cvd.split(",")[local].strip().isdigit() else local
+    done_layers = [0]
+
+    def count(res):
+        done_layers[0] += len(res)
     with ClockSampler(phys) as clk:
         l0 = lib.ic_launch_count()
         g0 = lib.ic_inverse_graph_count()
@@ -310,22 +406,23 @@ def run_device(args, rank: int, world: int) -> None:
         torch.cuda.synchronize(dev)
         e0.record()
         pool.fork()
-        for i in range(args.steps):
-            step(i)
-        pool.join()
+        run_model_steps(args, "t", args.steps, layers, order, fetch, pool, world, dev, on_gathered=count)
         e1.record()
         torch.cuda.synchronize(dev)
         launches = lib.ic_launch_count() - l0
         graphs = lib.ic_inverse_graph_count() - g0
     pool.check()
+    if rank == 0 and done_layers[0] != args.steps * len(layers):
+        raise RuntimeError(f"rank 0 holds {done_layers[0]} layer results, expected {args.steps * len(layers)}")
     if world > 1:
         torch.distributed.barrier()
     ms_max = max_over_ranks(e0.elapsed_time(e1), dev)
-    value = PARAMS_PER_SET * args.steps * world / (ms_max * 1e-3) / 1e6
+    value = n_params * args.steps / (ms_max * 1e-3) / 1e6
+    launches = int(max_over_ranks(float(launches), dev)) if world > 1 else int(launches)
     del sets
     torch.cuda.empty_cache()
 
-    e2e = run_e2e(args, dev, pool, world)
+    e2e = run_e2e(args, dev, pool, rank, world, layers, order)
     if rank != 0:
         return
     achieved, gemm_ms = dominant_gemm_tflops(dev)
@@ -336,90 +433,108 @@ def run_device(args, rank: int, world: int) -> None:
         pass
     bf16 = peaks.get("bf16_tflops", 1590.0)
     peak = bf16 / 2.0 / 3.0  # TF32 runs at half the bf16 rate; 3xTF32 issues three products
-    cpu_ts, cpu_params, cpu_kind = cpu_sample_seconds(1)
-    cpu_val = cpu_params / cpu_ts[0] / 1e6
+    bf16_s = peaks.get("bf16_tflops_sustained", 1400.0)
+    peak_s = bf16_s / 2.0 / 3.0
+    cpu = reference_cpu_subprocess(1, 0, 0.0, "proj")
+    ms_step = ms_max / args.steps
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 inverse; TF32 products with fp32 accumulation for the GPTQ trailing update)", "data": "synthetic",
-        "config": dict(CONFIG, parallelism=f"layer sets sharded over {world} GPU(s), no collective",
-                       streams=args.streams),
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (3xTF32 inverse; TF32 products with fp32 accumulation for the GPTQ trailing update)",
+        "data": "synthetic",
+        "config": dict(CONFIG, parallelism=f"{world} GPU(s): layers from a work queue (longest first), outputs "
+                                           f"gathered to rank 0 over NCCL", streams=args.streams,
+                       model_sets=args.model_sets, params=n_params, order=args.order),
         "e2e": e2e,
-        "gpu_launches": int(launches),
+        "gpu_launches": launches,
         "inverse_graphs_instantiated_in_timed_region": int(graphs),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": TRAFFIC_BYTES,
-                     "kernel": "gemm_tn_kernel<128,3> (3xTF32), 16384^3 product of the mlp_down inverse, "
-                               f"{gemm_ms:.2f} ms/launch",
+                     "kernel": "gemm_tn_kernel<128,3> (3xTF32), triangular U*U^T of the mlp_down inverse "
+                               f"(16384^3/3 flop), {gemm_ms:.2f} ms/launch",
                      "peak_basis": ("measured bf16 burst / 2 (TF32 rate) / 3 (3xTF32 products), of measured"
                                     if "bf16_tflops" in peaks else "fallback 1.59 PF bf16 / 2 / 3, of fallback")},
-        "step_roofline": {"bound": "tensor", "flop_per_step": FLOP_PER_SET,
-                          "target_ms": round(FLOP_PER_SET / (peak * 1e12) * 1e3, 3),
-                          "ms_per_step": round(ms_max / args.steps, 3),
-                          "frac": round(FLOP_PER_SET / (peak * 1e12) * 1e3 / (ms_max / args.steps), 4),
-                          "note": "whole step's algorithmic flop over the 3xTF32 peak, of measured"},
-        "cpu_baseline": {"value": round(cpu_val, 4), "unit": "Mparams/s", "cores": torch.get_num_threads(),
-                         "kind": cpu_kind,
-                         "sample": "one proj layer [4096,4096] through the reference's CPU calls (rotate_weights, "
-                                   "rotate_hessian, gptq_quantize_layer, pack_int4; baseline/_ref) or, when it "
-                                   "is not installed, oracle/cpu_ref.py"},
+        "step_roofline": {"bound": "tensor", "flop_per_step": n_flop,
+                          "target_ms": round(n_flop / (world * peak_s * 1e12) * 1e3, 3),
+                          "ms_per_step": round(ms_step, 3),
+                          "frac": round(n_flop / (world * peak_s * 1e12) * 1e3 / ms_step, 4),
+                          "note": "whole step's algorithmic flop over N x the sustained 3xTF32 peak "
+                                  "(bf16_tflops_sustained / 2 / 3), of measured"},
+        "cpu_baseline": (cpu["cpu_baseline"] if cpu else {"value": None, "unavailable": "reference not installed"}),
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) of the 16384^3 3xTF32 product timed by dominant_gemm_tflops (its four
-# K-slab launches together), from the ncu capture in profiles/gemm_tn_3xtf32_16384_traffic.md
-TRAFFIC_BYTES = 77_440_000_000
+# DRAM bytes (read + write) of the 16384^3 3xTF32 product timed by dominant_gemm_tflops, from
+# the ncu captures summarised in profiles/ (null until captured for the triangular product)
+TRAFFIC_BYTES = None
 
 
-def run_e2e(args, dev: torch.device, pool, world: int) -> dict:
-    """Same metric through the public API with HOST buffers: every step copies one
-    set's fp16 weights and fp32 Hessians from pinned host memory, quantizes, and
-    reads back the packed codes, scales and zero-points."""
+def run_e2e(args, dev: torch.device, pool, rank: int, world: int, layers, order) -> dict:
+    """The same metric through the public API with HOST buffers: every step copies
+    each layer's fp16 weight, fp32 Hessian and activation amax from pinned host
+    memory (LayerStreams' copy streams), quantizes, gathers the outputs to rank 0
+    and copies every layer's packed codes, scales, zero-points and statistics to
+    pinned host memory on rank 0; all inside the timed region."""
+    n_host = max(1, min(args.host_sets, args.model_sets))
     host = []
-    for name, W, H in make_set(99, dev):
-        host.append((name, W.cpu().pin_memory(), H.cpu().pin_memory()))
+    for i in range(n_host):
+        hs = {}
+        for name, W, H, a in make_set(5000 + 100 * rank + i, dev):
+            hs[name] = (W.cpu().pin_memory(), H.cpu().pin_memory(), a.cpu().pin_memory())
+        host.append(hs)
     torch.cuda.empty_cache()
-    res = {}
-    for name, m, n in LAYERS:
-        res[name] = (torch.empty(m, n // 2, dtype=torch.uint8).pin_memory(),
-                     torch.empty(m, 1, dtype=torch.float16).pin_memory(),
-                     torch.empty(m, 1, dtype=torch.int8).pin_memory())
-    h2d = sum(W.numel() * 2 + H.numel() * 4 for _, W, H in host)
-    d2h = sum(p.numel() + s.numel() * 2 + z.numel() + 3 * 8 for p, s, z in res.values())
+    specs = output_specs(layers)
+    outs = {}
+    if rank == 0:
+        for i in range(len(layers)):
+            outs[i] = {k: torch.empty(shape, dtype=dt).pin_memory() for k, (shape, dt) in specs(i).items()}
+    h2d = sum(m * n * 2 + n * n * 4 + n * 4 for _, _, m, n in layers)
+    d2h = sum(sum(t.numel() * t.element_size() for t in o.values()) for o in outs.values())
     steps = max(1, min(args.steps, args.e2e_steps))
 
-    st = {name: torch.empty(3, dtype=torch.float64).pin_memory() for name, _, _ in LAYERS}
+    def fetch(i):
+        si, name, _, _ = layers[i]
+        W, H, amax = host[si % n_host][name]
+        kw = dict(rot_size=ROT, block_size=BLOCK, damping=DAMP)
+        if name == "mlp_down":
+            kw["before"] = smoothrot_hook(amax)
+        if world == 1:
+            def then(o, i=i):
+                for k, t in outs[i].items():
+                    t.copy_(o[k], non_blocking=True)
+            kw["then"] = then
+        return W, H, kw
 
-    def step():
-        for name, Wh, Hh in host:
-            p, s, z = res[name]
+    def to_host(res):
+        if world > 1 and rank == 0:
+            for i, o in res.items():
+                for k, t in outs[i].items():
+                    t.copy_(o[k], non_blocking=True)
 
-            def fetch(o, p=p, s=s, z=z, name=name):
-                p.copy_(o["packed"], non_blocking=True)
-                s.copy_(o["scales"], non_blocking=True)
-                z.copy_(o["zero_points"], non_blocking=True)
-                st[name].copy_(o["stats"], non_blocking=True)
-            pool.submit(Wh, Hh, rot_size=ROT, block_size=BLOCK, damping=DAMP, then=fetch)
-
-    with pool:
-        step()
+    pool.fork()
+    run_model_steps(args, "ew", 1, layers, order, fetch, pool, world, dev, on_gathered=to_host)
+    pool.check()
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     pool.fork()
-    for _ in range(steps):
-        step()
+    run_model_steps(args, "et", steps, layers, order, fetch, pool, world, dev, on_gathered=to_host)
     pool.join()
     e1.record()
     torch.cuda.synchronize(dev)
     pool.check()
-    val = PARAMS_PER_SET * steps * world / (max_over_ranks(e0.elapsed_time(e1), dev) * 1e-3) / 1e6
-    return {"value": round(val, 3), "unit": "Mparams/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "steps": steps, "api": "int_crush_converter_b200.LayerStreams.submit -> quantize_gptq_layer (C ABI ic_gptq_layer)"}
+    n_params = sum(m * n for _, _, m, n in layers)
+    val = n_params * steps / (max_over_ranks(e0.elapsed_time(e1), dev) * 1e-3) / 1e6
+    return {"value": round(val, 3), "unit": "Mparams/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "host_sets": n_host,
+            "api": "int_crush_converter_b200.sharding.WorkQueue + LayerStreams.submit -> quantize_gptq_layer "
+                   "(C ABI ic_gptq_layer) with pinned host inputs; gather_results to rank 0; D2H of every "
+                   "layer's outputs on rank 0"}
 
 
 def run_hbm_kernels(reps: int = 5) -> None:
@@ -569,11 +684,17 @@ def run_configs() -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=24)
+    ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--sets", type=int, default=8, help="distinct resident sets per GPU (cycled)")
-    ap.add_argument("--e2e-steps", type=int, default=12)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cpu"])
+    ap.add_argument("--sets", type=int, default=8, help="distinct resident input sets per GPU (cycled)")
+    ap.add_argument("--host-sets", type=int, default=2, help="distinct pinned host input sets per GPU (e2e)")
+    ap.add_argument("--model-sets", type=int, default=MODEL_SETS, help="linear sets in the model (config 5: 40)")
+    ap.add_argument("--order", default="lpt", choices=["lpt", "natural"], help="work-queue order of the layers")
+    ap.add_argument("--depth", type=int, default=6, help="layers a rank keeps unfinished on its GPU")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--ref-sample", default="set", choices=["set", "proj"],
+                    help="reference CPU arm: time whole sets or the proj layer only")
     ap.add_argument("--ref-budget", type=float, default=150.0,
                     help="reference arm: stop the timed sets after this many seconds (at least one set)")
     ap.add_argument("--streams", type=int, default=4, help="CUDA streams the layers are issued on")
@@ -595,7 +716,7 @@ def main() -> None:
         s = make_set(0, dev)
         torch.cuda.synchronize(dev)
         with B.LayerStreams(args.streams, dev) as pool:
-            for _, W, H in s:
+            for _, W, H, _ in s:
                 pool.submit(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP)
         torch.cuda.synchronize(dev)
         print(json.dumps({"one_step": "ok", "layers": len(s)}))
@@ -610,6 +731,9 @@ def main() -> None:
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference-cpu":
+        run_reference_cpu(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

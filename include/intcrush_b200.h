@@ -228,7 +228,12 @@ int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw
  * column loop, pack, verify statistics.  smoothing (fp32 [N_in] or NULL):
  * the SmoothRot pre-step of pipeline.py:547-553 + 766-774, W[:, j] * s_j and
  * H[i,j] / max(s_i s_j, 1e-16) capped at 1e30 (pipeline.py:99-137), fused
- * into the rotation loads (needs 16 <= rot <= 512).  H fp32 [N_in, N_in] (already in the
+ * into the rotation loads (needs 16 <= rot <= 512).  smooth_order (with smoothing): 0
+ * smooths H and rotates it once (R^T diag(1/s) H diag(1/s) R, the Hessian of the
+ * smoothed-then-rotated weights); 1 follows the pipeline's own sequence for a
+ * SmoothRot layer, which rotates H before smoothing and again after it
+ * (pipeline.py:721-723 then 766-770: R^T diag(1/s) (R^T H R) diag(1/s) R; needs
+ * N_in % rot == 0).  H fp32 [N_in, N_in] (already in the
  * rotated space when h_rotated != 0).  Outputs: packed uint8 [M, npad/2]
  * (bits 4) and/or codes int8 [M, npad]; scales_f16 [M]; zp int8 [M] (bits 4
  * or asym).  With stats (fp64 [3] = {mse, max_err, status}: the pipeline's
@@ -242,7 +247,8 @@ int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw
  * on the parity aggregates; 1 does a third of the update's tensor work. */
 size_t ic_gptq_layer_workspace_size(int64_t M, int64_t N_in, int rot);
 int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, int64_t ldw, const float* H,
-                  int64_t ldh, const float* smoothing, int h_rotated, int rot, int bits, int asym, int block_size,
+                  int64_t ldh, const float* smoothing, int smooth_order, int h_rotated, int rot, int bits,
+                  int asym, int block_size,
                   float damping, int update_passes, int8_t* codes, uint8_t* packed, uint16_t* scales_f16,
                   int8_t* zp, double* stats, void* workspace, size_t workspace_bytes,
                   void* stream);

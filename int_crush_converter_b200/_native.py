@@ -68,7 +68,7 @@ SIGNATURES = {
     "ic_gptq_run_noalloc": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp,
                                    _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _vp]),
     "ic_gptq_layer_workspace_size": (_sz, [_i64, _i64, _i32]),
-    "ic_gptq_layer": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32,
+    "ic_gptq_layer": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
                              _f32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ic_ldlq_run": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _i64, _i32, _i32,
                            _vp, _i64, _i32, _vp, _sz, _vp]),

@@ -712,7 +712,8 @@ extern "C" size_t ic_gptq_layer_workspace_size(int64_t M, int64_t N_in, int rot)
 }
 
 extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, int64_t ldw_in, const float* H,
-                             int64_t ldh_in, const float* smoothing, int h_rotated, int rot, int bits, int asym, int block_size, float damping,
+                             int64_t ldh_in, const float* smoothing, int smooth_order, int h_rotated, int rot, int bits,
+                             int asym, int block_size, float damping,
                              int update_passes,
                              int8_t* codes, uint8_t* packed, uint16_t* scales_f16, int8_t* zp_out, double* stats,
                              void* workspace, size_t workspace_bytes, void* stream) {
@@ -731,8 +732,18 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   if (h_rotated && N_in != npad) return fail(IC_ERR_INVALID, "pre-rotated Hessian needs in_features % rot_size == 0");
   IC_TRY(rotate_weights(W, dtype, M, N_in, ldw_in, rot, w.W0, ldw, st, WEIGHT_OUTLIER_CLAMP, smoothing));
   IC_CUDA(cudaMemcpyAsync(w.Wk, w.W0, (size_t)M * ldw * 4, cudaMemcpyDeviceToDevice, st));
+  if (smooth_order != 0 && smooth_order != 1) return fail(IC_ERR_INVALID, "smooth_order must be 0 or 1");
   if (h_rotated || r <= 1) {
     IC_TRY(split_tf32(H, npad, npad, ldh_in, w.Hh, w.Hl, ldw, st, smoothing));
+  } else if (smoothing && smooth_order == 1) {
+    // The pipeline's own order for a SmoothRot layer (pipeline.py:721-723, then
+    // 766-770): rotate H, smooth the rotated matrix, rotate again.  The first
+    // rotation lands in the inverse's scratch (its U pair holds npad x ldw floats
+    // and is written only later, by the inverse).
+    if (npad != N_in) return fail(IC_ERR_UNSUPPORTED, "smooth_order 1 needs in_features % rot_size == 0");
+    float* tmp = static_cast<float*>(w.inv);
+    IC_TRY(rotate_hessian(H, 1, N_in, ldh_in, rot, tmp, nullptr, npad, ldw, st));
+    IC_TRY(rotate_hessian(tmp, 1, npad, ldw, rot, w.Hh, w.Hl, npad, ldw, st, smoothing));
   } else {
     IC_TRY(rotate_hessian(H, 1, N_in, ldh_in, rot, w.Hh, w.Hl, npad, ldw, st, smoothing));
   }

@@ -255,7 +255,8 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
                         asymmetric: bool = False, block_size: int = 128, damping: float = 0.01,
                         h_rotated: bool = False, want_codes: bool = False, want_packed: bool = True,
                         out: dict | None = None, ws: LayerWorkspace | None = None, check: bool = True,
-                        update_passes: int = 1, smoothing: torch.Tensor | None = None) -> dict:
+                        update_passes: int = 1, smoothing: torch.Tensor | None = None,
+                        smoothing_order: str = "pipeline") -> dict:
     """Fused GPTQ layer on the GPU: pipeline.py:527-559 + 702-809 + 919-931 + 1010-1013
     (outlier sanitize |w| > 1000 -> 0, rotations, GPTQ, packing, verify).
 
@@ -277,7 +278,11 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
     0.15%.  ``smoothing`` (per-input-channel factors s, [in]) applies the
     SmoothRot pre-step the pipeline runs on FFN down layers
     (pipeline.py:547-553 + 766-774): W[:, j] * s_j and H[i, j] / (s_i s_j)
-    before both rotations, fused into their loads.
+    before both rotations, fused into their loads.  ``smoothing_order``
+    "pipeline" (default) gives the Hessian the sequence the reference pipeline
+    actually runs for such a layer -- rotate, smooth, rotate again
+    (pipeline.py:721-723 then 766-770) -- so that results match it;
+    "smooth_then_rotate" rotates the smoothed Hessian once.
     """
     dev = device_of(W, H)
     Wd = W.to(dev)
@@ -313,8 +318,11 @@ def quantize_gptq_layer(W: torch.Tensor, H: torch.Tensor, rot_size: int = 256, i
         sm = f32(smoothing, dev).reshape(-1).contiguous()
         if sm.numel() != N:
             raise ValueError(f"smoothing has {sm.numel()} factors for {N} input features")
+    orders = {"smooth_then_rotate": 0, "pipeline": 1}
+    if smoothing_order not in orders:
+        raise ValueError(f"smoothing_order must be one of {list(orders)}, got {smoothing_order!r}")
     nat.check(lib.ic_gptq_layer(Wd.data_ptr(), _DT[Wd.dtype], M, N, N, Hd.data_ptr(), Hd.shape[1], nat.ptr(sm),
-                                int(h_rotated),
+                                orders[smoothing_order], int(h_rotated),
                                 rot_size, int_bits, int(asymmetric), block_size, float(damping), int(update_passes),
                                 nat.ptr(codes),
                                 nat.ptr(packed), s16.data_ptr(), nat.ptr(zp), stats.data_ptr(), wbuf.data_ptr(),
@@ -389,12 +397,15 @@ class LayerStreams:
         for s in self.streams + self.copy_streams:
             cur.wait_stream(s)
 
-    def submit(self, W: torch.Tensor, H: torch.Tensor, then=None, **kw) -> dict:
+    def submit(self, W: torch.Tensor, H: torch.Tensor, then=None, before=None, **kw) -> dict:
         """Issue :func:`quantize_gptq_layer` (same keyword arguments) on the least
         loaded stream; host inputs are copied to the device on that stream
-        (asynchronously when pinned; keep them alive until :meth:`join`), and
-        ``then(result)`` runs on that stream right after (e.g. a copy of the
-        outputs to host memory).  Returns the (asynchronous) result."""
+        (asynchronously when pinned; keep them alive until :meth:`join`).
+        ``before(W_device)`` runs on that stream first and returns extra keyword
+        arguments for the layer call (e.g. SmoothQuant factors computed on the
+        device); ``then(result)`` runs on that stream right after (e.g. a copy of
+        the outputs to host memory).  Returns the (asynchronous) result; its
+        ``done`` entry is a CUDA event recorded after the layer."""
         M, N = int(W.shape[0]), int(W.shape[1])
         i = min(range(len(self.load)), key=self.load.__getitem__)
         self.load[i] += float(M) * N * N + float(N) ** 3
@@ -413,11 +424,14 @@ class LayerStreams:
         for t in (W, H):
             t.record_stream(s)
         with torch.cuda.stream(s):
+            if before is not None:
+                kw = dict(kw, **before(W))
             res = quantize_gptq_layer(W, H, ws=self.ws[i], check=False, **kw)
             if then is not None:
                 then(res)
             ev = torch.cuda.Event()
             ev.record(s)
+        res["done"] = ev
         self._done[i] = self._done[i][-1:] + [ev]
         self._stats.append(res["stats"])
         return res

@@ -78,6 +78,121 @@ def quantize_layers_sharded(layers: Mapping[str, tuple[torch.Tensor, torch.Tenso
     return out
 
 
+def _default_store():
+    """The key-value store of the initialised default process group (the rendezvous
+    TCPStore under torchrun), or None without one."""
+    if not (torch.distributed.is_available() and torch.distributed.is_initialized()):
+        return None
+    from torch.distributed import distributed_c10d as c10d
+    return c10d._get_default_store()
+
+
+class WorkQueue:
+    """Work items handed out one at a time, in a fixed order (longest first), to
+    whichever rank asks next: the next index is an atomic counter in the process
+    group's key-value store (``store.add``), so a rank that runs ahead takes more
+    of the remaining layers (list scheduling) and a slow GPU -- these machines
+    are shared -- takes fewer, instead of every rank following a precomputed
+    table.  Each round of work uses its own ``key``.  Without a process group it
+    is a local counter."""
+
+    def __init__(self, order: Sequence[int], key: str, store=None):
+        self.order = list(order)
+        self.key = f"icq/{key}"
+        self.store = store if store is not None else _default_store()
+        self._local = 0
+
+    def take(self) -> int | None:
+        if self.store is None:
+            i = self._local
+            self._local += 1
+        else:
+            i = int(self.store.add(self.key, 1)) - 1
+        return self.order[i] if i < len(self.order) else None
+
+
+def longest_first(costs: Sequence[float]) -> list[int]:
+    """Indices by descending cost (ties by index)."""
+    return sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+
+
+def quantize_from_queue(queue: WorkQueue, fetch, pool, depth: int = 6) -> dict[int, dict]:
+    """Pull layers from `queue` and issue them on `pool` (a LayerStreams) until
+    the queue is empty.  ``fetch(i)`` returns (W, H, kwargs) of layer i (kwargs
+    may hold ``before`` / ``then`` hooks and the layer call's keyword
+    arguments).  A rank takes its next layer only while fewer than `depth` of
+    its layers are unfinished on the GPU, so the queue hands the rest to ranks
+    that are ahead.  Returns index -> asynchronous result for the layers this
+    rank quantized."""
+    inflight: list = []
+    out: dict[int, dict] = {}
+    while True:
+        while len(inflight) >= depth:
+            inflight.pop(0).synchronize()
+        i = queue.take()
+        if i is None:
+            return out
+        W, H, kw = fetch(i)
+        res = pool.submit(W, H, **kw)
+        out[i] = res
+        inflight.append(res["done"])
+
+
+def owner_table(mine: Iterable[int], n: int, device=None) -> list[int]:
+    """Which rank holds each of `n` items (-1: none), from each rank's own list
+    (one MAX all-reduce of an int32 vector)."""
+    rank, world = _group_info(None)
+    t = torch.full((n,), -1, dtype=torch.int32, device=device)
+    idx = list(mine)
+    if idx:
+        t[torch.tensor(idx, dtype=torch.long, device=device)] = rank
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
+def gather_results(results: dict[int, dict], n: int, specs, dst: int = 0,
+                   keys: Sequence[str] = ("packed", "scales", "zero_points", "stats"), device=None) -> dict[int, dict]:
+    """Bring every layer's outputs to rank `dst` (point-to-point sends over the
+    process group: NVLink with NCCL).  ``results`` are this rank's (index ->
+    dict of device tensors); ``specs(i)`` gives {key: (shape, dtype)} of layer
+    i's outputs, for the receive buffers.  On `dst` returns all n layers; on
+    other ranks, after their sends complete, an empty dict.  Call it after the
+    results are ready on the current stream (e.g. LayerStreams.join)."""
+    rank, world = _group_info(None)
+    if world == 1:
+        return dict(results)
+    owner = owner_table(results.keys(), n, device)
+    missing = [i for i, r in enumerate(owner) if r < 0]
+    if missing:
+        raise RuntimeError(f"gather_results: no rank holds layers {missing[:8]}")
+    ops = []
+    got: dict[int, dict] = {}
+    if rank == dst:
+        got = {i: results[i] for i in results}
+        for i in range(n):
+            if owner[i] == dst:
+                continue
+            bufs = {}
+            for k in keys:
+                shape, dtype = specs(i)[k]
+                if shape is None:
+                    bufs[k] = None
+                    continue
+                bufs[k] = torch.empty(shape, dtype=dtype, device=device)
+                ops.append(torch.distributed.P2POp(torch.distributed.irecv, bufs[k], owner[i]))
+            got[i] = bufs
+    else:
+        for i in sorted(results):
+            for k in keys:
+                if results[i].get(k) is not None:
+                    ops.append(torch.distributed.P2POp(torch.distributed.isend, results[i][k].contiguous(), dst))
+    if ops:
+        for w in torch.distributed.batch_isend_irecv(ops):
+            w.wait()
+    return got if rank == dst else {}
+
+
 def owners(names: Iterable[str], shapes: Sequence[tuple[int, int]], world: int) -> dict[str, int]:
     """name -> owning rank, for gathering results on the host afterwards."""
     table = shard_layers([layer_cost(m, n) for m, n in shapes], world)

@@ -361,7 +361,7 @@ def test_gptq_layer_not_pd_reported():
     packed = torch.empty(M, N // 2, dtype=torch.uint8, device="cuda")
     s16 = torch.empty(M, dtype=torch.float16, device="cuda")
     zp = torch.empty(M, dtype=torch.int8, device="cuda")
-    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, None, 0, 256, 4, 0, 128, 0.01, 1, None,
+    st = lib.ic_gptq_layer(W.data_ptr(), nat.IC_F16, M, N, N, H.data_ptr(), N, None, 0, 0, 256, 4, 0, 128, 0.01, 1, None,
                            packed.data_ptr(), s16.data_ptr(), zp.data_ptr(), None, ws.data_ptr(), ws.numel(),
                            nat.stream_ptr(W.device))
     assert st == nat.IC_ERR_NOT_PD
@@ -632,18 +632,24 @@ def test_smoothing_mirrors_match_golden(golden):
     assert np.array_equal(np_(B._transform_hessian_for_smoothquant(cu(H), cu(s))), golden["smooth_basic/H_smooth"])
 
 
-def test_gptq_layer_with_smoothrot_vs_oracle():
+@pytest.mark.parametrize("order", ["smooth_then_rotate", "pipeline"])
+def test_gptq_layer_with_smoothrot_vs_oracle(order):
     """The fused SmoothRot pre-step (W * s and H / (s_i s_j) in the rotation
-    loads) against the oracle's smooth -> rotate -> GPTQ."""
+    loads) against the oracle's smooth -> rotate -> GPTQ; with order
+    "pipeline" the Hessian takes the reference pipeline's own sequence for a
+    SmoothRot layer, rotate -> smooth -> rotate (pipeline.py:721-723, 766-770)."""
     M, N = 256, 1024
     W = gi.weight_outlier_cols(600, M, N)
     H = gi.hessian_lognormal(601, N, 2 * N)
     s = np.exp(np.random.default_rng(602).normal(0.0, 0.5, N)).astype(np.float32)
     Wr = R.rotate_weights(R.apply_smoothing_to_weight(W, s), 256)
-    Hr = R.rotate_hessian(R.transform_hessian_for_smoothquant(H, s), 256)
+    if order == "pipeline":
+        Hr = R.rotate_hessian(R.transform_hessian_for_smoothquant(R.rotate_hessian(H, 256), s), 256)
+    else:
+        Hr = R.rotate_hessian(R.transform_hessian_for_smoothquant(H, s), 256)
     ref = R.gptq_quantize_layer(Wr, Hr, 128, 0.01, 4)
     out = B.quantize_gptq_layer(cu(W), cu(H), rot_size=256, want_codes=True,
-                                smoothing=cu(s))
+                                smoothing=cu(s), smoothing_order=order)
     q = np_(out["codes"])
     assert np.array_equal(np_(out["scales"]), ref["scales"])
     p = R.proxy_loss(Wr, q, ref["scales"].astype(np.float32), ref["zero_points"], Hr)

@@ -187,3 +187,64 @@ def test_two_gloo_ranks_source_failure_and_nan_stats():
         assert res[r][1] == 2
         assert res[r][2] == (2.0, True)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _queue_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=60))
+    try:
+        costs = [float(c) for c in (5, 1, 9, 3, 7, 2, 8)]
+        order = S.longest_first(costs)
+        wq = S.WorkQueue(order, "t0")
+        taken = []
+        while True:
+            i = wq.take()
+            if i is None:
+                break
+            taken.append(i)
+        # each rank "quantizes" its layers: outputs derived from the index
+        res = {i: {"packed": torch.full((2, 3), i, dtype=torch.uint8), "scales": torch.full((2, 1), float(i)),
+                   "zero_points": None, "stats": torch.tensor([i, 0.0, 0.0], dtype=torch.float64)} for i in taken}
+
+        def specs(i):
+            return {"packed": ((2, 3), torch.uint8), "scales": ((2, 1), torch.float32), "zero_points": (None, None),
+                    "stats": ((3,), torch.float64)}
+        got = S.gather_results(res, len(costs), specs, dst=0)
+        ok = rank != 0 or (sorted(got) == list(range(len(costs))) and all(
+            int(got[i]["packed"][1, 2]) == i and float(got[i]["scales"][0, 0]) == i and got[i]["zero_points"] is None
+            and float(got[i]["stats"][0]) == i for i in got))
+        q.put((rank, taken, ok))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_two_gloo_ranks_work_queue_and_gather():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_queue_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    taken0, taken1 = res[0][1], res[1][1]
+    assert not set(taken0) & set(taken1)
+    assert sorted(taken0 + taken1) == list(range(7))
+    assert res[0][2] and res[1][2]
+    # each rank takes in longest-first order
+    costs = [5, 1, 9, 3, 7, 2, 8]
+    for t in (taken0, taken1):
+        assert [costs[i] for i in t] == sorted((costs[i] for i in t), reverse=True)
+
+
+def test_work_queue_without_a_process_group():
+    wq = S.WorkQueue([2, 0, 1], "local")
+    assert [wq.take(), wq.take(), wq.take(), wq.take()] == [2, 0, 1, None]
