@@ -32,6 +32,7 @@ Modes:
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -436,6 +437,7 @@ def run_device(args, rank: int, world: int) -> None:
     bf16_s = peaks.get("bf16_tflops_sustained", 1400.0)
     peak_s = bf16_s / 2.0 / 3.0
     cpu = reference_cpu_subprocess(1, 0, 0.0, "proj")
+    dropin = run_dropin(dev) if args.dropin else None
     ms_step = ms_max / args.steps
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
@@ -447,6 +449,7 @@ def run_device(args, rank: int, world: int) -> None:
                                            f"gathered to rank 0 over NCCL", streams=args.streams,
                        model_sets=args.model_sets, params=n_params, order=args.order),
         "e2e": e2e,
+        "dropin_e2e": dropin,
         "gpu_launches": launches,
         "inverse_graphs_instantiated_in_timed_region": int(graphs),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
@@ -470,6 +473,36 @@ def run_device(args, rank: int, world: int) -> None:
 # DRAM bytes (read + write) of the 16384^3 3xTF32 product timed by dominant_gemm_tflops, from
 # the ncu captures summarised in profiles/ (null until captured for the triangular product)
 TRAFFIC_BYTES = None
+
+
+def run_dropin(dev: torch.device, reps: int = 2) -> dict:
+    """The same metric through the reference pipeline's own per-layer call
+    shape with this package installed in its place (pipeline_hook): per layer
+    rotate_weights(W) -> rotate_hessian(H) -> gptq_quantize_layer(W_rot, H_rot)
+    -> pack_int4(q), every call on host tensors as the pipeline passes them (W
+    upcast to fp32 on the host, pipeline.py:524), each call copying in and
+    out.  One config-3 set per rep, rank 0 only."""
+    import int_crush_converter_b200 as B
+    host = [(name, W.float().cpu(), H.cpu()) for name, W, H, _ in make_set(77, dev)]
+    torch.cuda.empty_cache()
+
+    def one_set():
+        for _, W, H in host:
+            Wr = B.rotate_weights(W, ROT)
+            Hr = B.rotate_hessian(H, ROT)
+            r = B.gptq_quantize_layer(Wr, Hr, block_size=BLOCK, damping=DAMP, int_bits=4)
+            B.pack_int4(r.quantized_W)
+    one_set()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one_set()
+    torch.cuda.synchronize(dev)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(PARAMS_PER_SET / dt / 1e6, 3), "unit": "Mparams/s", "seconds_per_set": round(dt, 3),
+            "sets": reps, "api": "reference call shape: rotate_weights -> rotate_hessian -> gptq_quantize_layer "
+                                 "-> pack_int4 on CPU tensors (pipeline.py:547-559, 702-789, 1010-1013), "
+                                 "one layer at a time, host wall clock"}
 
 
 def run_e2e(args, dev: torch.device, pool, rank: int, world: int, layers, order) -> dict:
@@ -543,6 +576,8 @@ def run_hbm_kernels(reps: int = 5) -> None:
     Algorithmic bytes (the minimum a kernel must move):
       rtn_fused (config 1: fp16 W [4096,4096] x 8 layers, INT4 sym rot256):
           2 B read + 0.5 B packed written per weight (+ 2 B scale per row)
+      rtn_fused (config 2: fp16 W, 16 x [3072,3072] + 16 x [12288,3072], INT8 sym rot64, 5 ratios):
+          2 B read + 1 B codes written per weight (+ 2 B scale per row)
       rotate_weights (fp16 -> fp32 rot256, [4096,16384]): 2 B read + 4 B written per weight
       rotate_hessian (fp32 H [16384,16384] -> rotated TF32 hi/lo pair, rot256):
           4 B read + 8 B written per element"""
@@ -585,9 +620,28 @@ def run_hbm_kernels(reps: int = 5) -> None:
             nat.check(lib.ic_rtn_fused(W.data_ptr(), nat.IC_F16, 4096, 4096, 4096, 256, 4, 0, None, 0, None,
                                        packed.data_ptr(), sc.data_ptr(), None, sq.data_ptr(), mx.data_ptr(), st))
     ms, gbs, frac = timed(rtn, 8 * (4096 * 4096 * 2.5 + 4096 * 2))
-    out.append(dict(kernel="rtn_regs_kernel (ic_rtn_fused)", workload="config 1: 8 x fp16 [4096,4096] INT4 sym rot256",
+    out.append(dict(kernel="rtn_fast_kernel<half,256> (ic_rtn_fused)", workload="config 1: 8 x fp16 [4096,4096] INT4 sym rot256",
                     ms_per_call=ms, achieved_gbs=gbs, frac=frac))
     del Ws
+    # config 2: RTN INT8 sym rot64 with the 5-ratio clip search, 16 x [3072,3072] + 16 x [12288,3072]
+    ratios = (ctypes.c_float * 5)(0.8, 0.85, 0.9, 0.95, 1.0)
+    W2 = [(torch.randn(m, 3072, generator=g, device=dev) * 0.02).half() for m in [3072] * 16 + [12288] * 16]
+    c2 = torch.empty(12288, 3072, dtype=torch.int8, device=dev)
+    sc2 = torch.empty(12288, dtype=torch.float16, device=dev)
+    sq2 = torch.empty(12288, dtype=torch.float64, device=dev)
+    mx2 = torch.empty(12288, dtype=torch.float32, device=dev)
+    p2 = sum(W.shape[0] * 3072 for W in W2)
+
+    def rtn8():
+        for W in W2:
+            m = W.shape[0]
+            nat.check(lib.ic_rtn_fused(W.data_ptr(), nat.IC_F16, m, 3072, 3072, 64, 8, 0, ratios, 5, c2.data_ptr(),
+                                       None, sc2.data_ptr(), None, sq2.data_ptr(), mx2.data_ptr(), st))
+    ms, gbs, frac = timed(rtn8, p2 * 3 + sum(W.shape[0] for W in W2) * 2)
+    out.append(dict(kernel="rtn_fast_kernel<half,64> (ic_rtn_fused)",
+                    workload="config 2: 16 x [3072,3072] + 16 x [12288,3072] fp16, INT8 sym rot64, 5 clipping ratios",
+                    ms_per_call=ms, achieved_gbs=gbs, frac=frac))
+    del W2, c2
     W = (torch.randn(4096, 16384, generator=g, device=dev) * 0.02).half()
     Wr = torch.empty(4096, 16384, device=dev)
 
@@ -692,6 +746,7 @@ def main() -> None:
     ap.add_argument("--model-sets", type=int, default=MODEL_SETS, help="linear sets in the model (config 5: 40)")
     ap.add_argument("--order", default="lpt", choices=["lpt", "natural"], help="work-queue order of the layers")
     ap.add_argument("--depth", type=int, default=6, help="layers a rank keeps unfinished on its GPU")
+    ap.add_argument("--dropin", type=int, default=1, help="also time the reference call shape (drop-in API)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--ref-sample", default="set", choices=["set", "proj"],
                     help="reference CPU arm: time whole sets or the proj layer only")
@@ -705,9 +760,27 @@ def main() -> None:
     ap.add_argument("--one-step", action="store_true",
                     help="quantize one set once and exit (for an ncu launch list of exactly one step)")
     ap.add_argument("--configs", action="store_true", help="time BASELINE configs 1, 2 and 4 and exit")
+    ap.add_argument("--profile-layer", default="",
+                    help="M,N: quantize one synthetic GPTQ layer [M,N] twice (one warm-up) and exit -- a small "
+                         "case for kernel captures")
     args = ap.parse_args()
     if args.configs:
         run_configs()
+        return
+    if args.profile_layer:
+        import int_crush_converter_b200 as B
+        m, n = (int(x) for x in args.profile_layer.split(","))
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        g = torch.Generator(device=dev).manual_seed(5)
+        W = (torch.randn(m, n, generator=g, device=dev) * 0.02).half()
+        X = torch.randn(N_SAMPLES, n, generator=g, device=dev) * torch.exp(torch.randn(n, generator=g, device=dev))
+        H = X.T @ X / N_SAMPLES
+        del X
+        for _ in range(2):
+            B.quantize_gptq_layer(W, H, rot_size=ROT, block_size=BLOCK, damping=DAMP)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_layer": [m, n], "ok": True}))
         return
     if args.one_step:
         import int_crush_converter_b200 as B

@@ -179,6 +179,36 @@ int ic_spd_cholesky(float* h_hi, float* h_lo, int64_t n, int64_t ldh, void* work
 int ic_smooth_factors(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, const float* act,
                       int64_t act_stride, int mode, float alpha, float nsamp, float* out, void* stream);
 
+/* PermuQuant candidate order (converter/permuquant.py:13-67): key[j] = the second
+ * moment mean_i W[i,j]^2 of input channel j (fp64 sum, fp32 result), or with
+ * act_mu2 != NULL the joint key max(act_mu2[j],1e-12)^alpha *
+ * max(key[j],1e-12)^(1-alpha); perm int32 [N] = channels by descending key,
+ * ties by index (a stable argsort(descending=True)).  W fp16/bf16/fp32 [M, N]. */
+int ic_permuquant_order(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, const float* act_mu2,
+                        float alpha, float* key, int32_t* perm, void* stream);
+
+/* compute_group_quant_error (converter/permuquant.py:70-105) of W, or of
+ * W[:, perm] when perm != NULL (inv_scratch int32 [N] then receives the
+ * inverse permutation): RTN with fp16 per-group scales (bits 4: group_size,
+ * absmax/7; bits 8: per row, absmax/127), round-half-away codes, and per row
+ * the sum of squared errors, each term exact in fp64, summed in the original
+ * column order (so with groups spanning the row a permutation gives the same
+ * sums bit for bit).  row_err fp64 [M]. */
+int ic_group_quant_error(const void* W, int dtype, int64_t M, int64_t N, int64_t ldw, const int32_t* perm,
+                         int64_t group_size, int bits, int32_t* inv_scratch, double* row_err, void* stream);
+
+/* --------------------------------------- SVD-absorbed split (svd.py:35-75) */
+/* The small dense steps of the randomized low-rank SVD that
+ * svd.decompose_weight calls (torch.svd_lowrank, q = rank, niter = 2); its
+ * products run on ic_gemm_tn.  ic_orthonormalize: the columns of X [m, q]
+ * (row-major, leading dimension ldx, 1 <= q <= min(m, 64)) made orthonormal in
+ * place (modified Gram-Schmidt, twice, fp64 sums) -- the range finder's QR.
+ * ic_sym_eig: eigenvalues (descending) and eigenvectors (columns of V) of a
+ * symmetric q x q matrix, q <= 64, by cyclic Jacobi -- the SVD of the
+ * projected matrix through B B^T. */
+int ic_orthonormalize(float* X, int64_t m, int q, int64_t ldx, void* stream);
+int ic_sym_eig(const float* A, int q, int64_t lda, float* evals, float* V, int64_t ldv, void* stream);
+
 /* ------------------------------------------------------------------- GPTQ */
 /* Per-row scale / zero-point preparation of gptq_quantize_layer
  * (converter/gptq.py:254-317): bits 4 -> asymmetric range scales with the
@@ -237,8 +267,11 @@ int ic_gptq_run_noalloc(float* W_work, int64_t ldw, const float* W0, int64_t ldw
  * rotated space when h_rotated != 0).  Outputs: packed uint8 [M, npad/2]
  * (bits 4) and/or codes int8 [M, npad]; scales_f16 [M]; zp int8 [M] (bits 4
  * or asym).  With stats (fp64 [3] = {mse, max_err, status}: the pipeline's
- * verify statistics and the layer's status bits, 2 = Hessian not positive
- * definite) the call does not synchronise and the caller checks stats[2]
+ * verify statistics and the layer's status bits: 2 = Hessian not positive
+ * definite, 8 = a row's fp16 scale is NaN, infinite or zero, the condition on
+ * which the pipeline repairs scales, pipeline.py:935-1007; for the only
+ * reachable case, a NaN weight, the outputs already equal the repaired ones:
+ * NaN scale, zero-point 0, codes 0) the call does not synchronise and the caller checks stats[2]
  * (the reference then takes its inv/pinv branch); with stats == NULL it
  * synchronises once and returns IC_ERR_NOT_PD.  update_passes: the lazy
  * trailing update W -= E * Hinv (rounding.py:100-103) as 1 = TF32 products

@@ -32,3 +32,8 @@ from .smoothquant import (  # noqa: E402,F401
     apply_smoothing_to_weight, _transform_hessian_for_smoothquant, compute_smoothing_factors,
     compute_smoothing_from_hessian_diag,
 )
+from .permuquant import (  # noqa: E402,F401
+    channel_second_moments, compute_group_quant_error, find_permutation_joint, find_permutation_weight,
+    find_permutation_with_acceptance, sweep_alpha,
+)
+from .svd import SVDResult, decompose_weight  # noqa: E402,F401

@@ -22,6 +22,7 @@ IC_ERR_CUDA = -2
 IC_ERR_NOT_PD = -3
 DEV_TIMEOUT = 1
 DEV_NOT_PD = 2
+DEV_BAD_SCALE = 8  # a row's fp16 scale is NaN/inf/0 (the pipeline's bad-scale condition)
 IC_ERR_TIMEOUT = -4
 IC_ERR_RANGE = -5
 IC_ERR_UNSUPPORTED = -6
@@ -61,6 +62,10 @@ SIGNATURES = {
     "ic_spd_inverse": (_i32, [_vp, _vp, _i64, _i64, _f32, _vp, _sz, _vp]),
     "ic_spd_cholesky": (_i32, [_vp, _vp, _i64, _i64, _vp, _sz, _vp]),
     "ic_smooth_factors": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i32, _f32, _f32, _vp, _vp]),
+    "ic_permuquant_order": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _f32, _vp, _vp, _vp]),
+    "ic_group_quant_error": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i32, _vp, _vp, _vp]),
+    "ic_orthonormalize": (_i32, [_vp, _i64, _i32, _i64, _vp]),
+    "ic_sym_eig": (_i32, [_vp, _i32, _i64, _vp, _vp, _i64, _vp]),
     "ic_gptq_row_params": (_i32, [_vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "ic_gptq_workspace_size": (_sz, [_i64, _i64, _i32, _i32]),
     "ic_gptq_run": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp,

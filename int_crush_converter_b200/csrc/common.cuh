@@ -70,7 +70,7 @@ unsigned long long launches();
   } while (0)
 
 // ---- device-side status word -------------------------------------------------
-enum : unsigned { DEV_TIMEOUT = 1u, DEV_NOT_PD = 2u, DEV_RANGE = 4u };
+enum : unsigned { DEV_TIMEOUT = 1u, DEV_NOT_PD = 2u, DEV_RANGE = 4u, DEV_BAD_SCALE = 8u };
 unsigned* device_flags();  // per-device word, allocated once at first use
 
 // Bounded wait on phase `parity` of a shared-memory mbarrier: true once the

@@ -39,6 +39,7 @@ struct GemmArgs {
   int group;  // row-tiles per group of the tile order
   int chunk;  // k-tiles per TMEM accumulator chunk (3xTF32)
   int kofs;  // K index of column 0 of A/B in the full product (K-slab launches)
+  int accum_in_place;  // D aliases C with beta == 1: a tile with K = 0 leaves D unchanged
   int tri;  // bit 0: only output tiles on/below the diagonal (n0 <= m0);
             // bit 1: A rows are zero left of their own index (upper triangular
             //        A), so the K loop starts at the tile's first row m0
@@ -349,6 +350,9 @@ __global__ void __launch_bounds__(384, 1)
     const int kbase = (args.tri & 2) ? min(max(m0 - args.kofs, 0), args.k) : 0;
     const int ktiles = (args.k - kbase + BK - 1) / BK;
     const int nchunks = C::CHUNKED ? (ktiles + CH - 1) / CH : (ktiles > 0 ? 1 : 0);
+    // a tile with nothing to add to D in place (a later K-slab of a triangular
+    // product below its rows) keeps D as it is: no epilogue read/write
+    if (ktiles == 0 && args.accum_in_place) continue;
 
     if (warp >= 4 && args.beta != 0.f && args.c_hi) {
       // warm L2 with this tile's C rows while the main loop runs
@@ -553,6 +557,7 @@ __global__ void __launch_bounds__(384, 1)
   const int kbase = (args.tri & 2) ? min(max(mp - args.kofs, 0), args.k) : 0;
   const int ktiles = (args.k - kbase + BK - 1) / BK;
   const int nchunks = (ktiles + CH - 1) / CH;
+  if (ktiles == 0 && args.accum_in_place) return;  // pair-uniform: D keeps its value
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -824,8 +829,9 @@ int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, c
                    (!c_lo || aligned16(c_lo)) && (!d_lo || aligned16(d_lo));
   unsigned* flags = device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
+  const int in_place = beta == 1.f && c_hi == d_hi && c_lo == d_lo && ldc == ldd;
   GemmArgs a{(int)m, (int)n, (int)(k > 0 ? k : 0), alpha, beta, c_hi, c_lo, (long long)ldc,
-             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tune_group(), tune_chunk(), kofs, tri};
+             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tune_group(), tune_chunk(), kofs, in_place, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
   if (passes == 3 && m > BM && pair_enabled()) {

@@ -453,14 +453,25 @@ __global__ void stats_kernel(const double* __restrict__ sq, const float* __restr
   }
 }
 
+// fp16 scales and int8 zero-points of the layer.  A row whose stored scale is
+// NaN, infinite or zero (only a NaN weight in the row can cause one: the scale
+// is clamped to [1e-5, 65500]) sets DEV_BAD_SCALE in `status`: the pipeline's
+// verify step flags such a layer and "repairs" its rows (pipeline.py:935-1007),
+// which for a NaN row reproduces the NaN scale, and zero zero-point and codes
+// (torch converts NaN to int8 0, as the conversions here do).
 __global__ void params_out_kernel(const float* __restrict__ s, const float* __restrict__ z, int64_t M,
-                                  uint16_t* __restrict__ s16, int8_t* __restrict__ z8, float* __restrict__ s16f) {
+                                  uint16_t* __restrict__ s16, int8_t* __restrict__ z8, float* __restrict__ s16f,
+                                  unsigned* status) {
+  bool bad = false;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M; i += (int64_t)gridDim.x * blockDim.x) {
     const __half h = __float2half_rn(s[i]);
+    const float hf = __half2float(h);
+    bad |= !(fabsf(hf) < INFINITY) || hf == 0.f;
     if (s16) s16[i] = __half_as_ushort(h);
-    if (s16f) s16f[i] = __half2float(h);
-    if (z8 && z) z8[i] = (int8_t)z[i];
+    if (s16f) s16f[i] = hf;
+    if (z8 && z) z8[i] = z[i] != z[i] ? (int8_t)0 : (int8_t)z[i];
   }
+  if (bad && status) atomicOr(status, DEV_BAD_SCALE);
 }
 
 // converter/ldlq.py:553-599, elementwise (floor/ceil from the caller)
@@ -749,12 +760,12 @@ extern "C" int ic_gptq_layer(const void* W, int dtype, int64_t M, int64_t N_in, 
   }
   const bool has_zp = bits == 4 || asym;
   IC_TRY(ic_gptq_row_params(w.W0, M, npad, ldw, bits, asym, w.scale, has_zp ? w.zp : nullptr, st));
-  params_out_kernel<<<grid1(M), 256, 0, st>>>(w.scale, has_zp ? w.zp : nullptr, M, scales_f16,
-                                               has_zp ? zp_out : nullptr, w.sscale);
-  IC_CHECK_LAUNCH();
-  // With stats the call stays asynchronous: the inverse's not-positive-definite bit lands in
-  // stats[2].  Without stats it synchronises once to return IC_ERR_NOT_PD.
+  // With stats the call stays asynchronous: the inverse's not-positive-definite bit (and the
+  // bad-scale bit) land in stats[2].  Without stats it synchronises once to return IC_ERR_NOT_PD.
   IC_CUDA(cudaMemsetAsync(w.status, 0, sizeof(unsigned), st));
+  params_out_kernel<<<grid1(M), 256, 0, st>>>(w.scale, has_zp ? w.zp : nullptr, M, scales_f16,
+                                               has_zp ? zp_out : nullptr, w.sscale, w.status);
+  IC_CHECK_LAUNCH();
   // The column loop reads Hinv's lower 128-tiles and its diagonal blocks; when
   // the block size divides 128 no block straddles a tile, so the upper tiles
   // are never read and the mirror pass is skipped.

@@ -155,15 +155,42 @@ __device__ __forceinline__ void cross2(float (&v)[16], int m, bool upper) {
 // The group Hadamard of 16 consecutive elements per lane, L = rot/16 lanes per
 // group (lane l of the group holds elements 16l .. 16l+15), all lanes of the
 // warp taking part (shfl_xor).  16 <= rot <= 512.
+// H4 without its factor 1/2, and cross4 likewise: the factors of all stages
+// are applied at once at the end (a power of two, so every intermediate is the
+// scaled twin of the per-stage result and the output is bit-identical).
+__device__ __forceinline__ void h4_unscaled(float& x0, float& x1, float& x2, float& x3) {
+  const float p = __fadd_rn(x0, x1), m = __fsub_rn(x0, x1);
+  const float P = __fadd_rn(x2, x3), Mm = __fsub_rn(x2, x3);
+  x0 = __fadd_rn(p, Mm);
+  x1 = __fsub_rn(p, Mm);
+  x2 = __fadd_rn(m, P);
+  x3 = __fsub_rn(P, m);
+}
+__device__ __forceinline__ void cross4_unscaled(float (&v)[16], int m) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float a1 = __shfl_xor_sync(0xffffffffu, v[j], m);
+    const float a2 = __shfl_xor_sync(0xffffffffu, v[j], 2 * m);
+    const float a3 = __shfl_xor_sync(0xffffffffu, v[j], 3 * m);
+    v[j] = __fadd_rn(__fadd_rn(v[j], a1), __fsub_rn(a2, a3));
+  }
+}
+
 __device__ __forceinline__ void hadamard_regs16(float (&v)[16], int rot, int l) {
   const int L = rot / 16;
   const bool p4 = is_pow4(rot);
   if (p4) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) h4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    for (int q = 0; q < 4; ++q) h4_unscaled(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) h4(v[q], v[4 + q], v[8 + q], v[12 + q]);
-    for (int m = 1; m < L; m <<= 2) cross4(v, m);
+    for (int q = 0; q < 4; ++q) h4_unscaled(v[q], v[4 + q], v[8 + q], v[12 + q]);
+    float scale = 0.25f;
+    for (int m = 1; m < L; m <<= 2) {
+      cross4_unscaled(v, m);
+      scale *= 0.5f;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], scale);
   } else {
 #pragma unroll
     for (int st = 1; st < 16; st <<= 1) {

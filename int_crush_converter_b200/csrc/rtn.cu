@@ -7,6 +7,8 @@
 // no contraction): scale = clamp(stat * ratio / divisor), fp16 storage,
 // candidate MSE with round-half-even (Tensor.round), final codes with
 // round-half-away-from-zero, strict-< ratio selection (first ratio wins ties).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "hadamard.cuh"
 #include "internal.h"
@@ -452,6 +454,308 @@ __global__ void __launch_bounds__(NT) rtn_regs_kernel(const RtnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fast path for the common shape of the fused RTN call: one scale per row,
+// a regular (power-of-four) rotation of 16, 64 or 256, rows of at most 4096
+// elements.  Same results as rtn_regs_kernel, fewer instructions per weight:
+//   * the Hadamard's 1/2 per radix-4 stage is deferred: the butterflies run on
+//     2^k-scaled values (k = log4(rot)); every quantity the kernel derives from
+//     them (absmax, quotients against the 2^k-scaled scale, errors, squared
+//     errors) is the unscaled one times a power of two, exactly, so codes,
+//     scales and statistics are bit-identical;
+//   * for rot 256 the two cross-lane digits go through one shared-memory
+//     transpose (16 stores + 4 vector loads per lane) instead of 6 shuffles per
+//     element, and the codes come back through a byte transpose for packing;
+//   * NaN-propagating max as one max.NaN instruction;
+//   * round-half-away-from-zero and the check for quotients next to a rounding
+//     boundary fused (floor by a round-down add of 1.5 * 2^23);
+//   * the clipping-ratio search takes the FMA-corrected quotient and its
+//     round-half-even by the same magic add, and falls back to the IEEE
+//     division only for quotients within 2^-14 of a tie.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float min_nan(float a, float b) {
+  float d;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+// y = RN(v / s) for the code's round-half-away, from rs = RN(1/s): corrected
+// quotient, then exact IEEE division when |y| + 1/2 lies within 2^-14 of an
+// integer (the only quotients whose code the last ulp can change).  Returns
+// the rounded magnitude floor(|y| + 1/2) as a float and y itself.
+__device__ __forceinline__ float fast_rhaz(float v, float s, float rs, float z, bool has_z) {
+  const float q0 = __fmul_rn(v, rs);
+  float y = __fmaf_rn(__fmaf_rn(-q0, s, v), rs, q0);
+  if (has_z) y = __fadd_rn(y, z);
+  const float t = __fadd_rn(fabsf(y), 0.5f);
+  float fl = __fsub_rn(__fadd_rd(t, 12582912.f), 12582912.f);  // floor(t), t < 2^22
+  const float d = __fsub_rn(t, fl);
+  if (!(t < 4194304.f) || d < 0x1p-14f || d > 1.f - 0x1p-14f) {
+    y = __fdiv_rn(v, s);
+    if (has_z) y = __fadd_rn(y, z);
+    return rhaz(y);
+  }
+  return copysignf(fl, y);
+}
+// round-half-even of RN(v / s) (Tensor.round in the clip search), same scheme
+__device__ __forceinline__ float fast_rint_div(float v, float s, float rs, float z, bool has_z) {
+  const float q0 = __fmul_rn(v, rs);
+  float y = __fmaf_rn(__fmaf_rn(-q0, s, v), rs, q0);
+  if (has_z) y = __fadd_rn(y, z);
+  const float r = __fsub_rn(__fadd_rn(y, 12582912.f), 12582912.f);  // RN-even, |y| < 2^22
+  const float d = fabsf(__fsub_rn(y, r));
+  if (!(fabsf(y) < 4194304.f) || d > 0.5f - 0x1p-14f) {
+    y = __fdiv_rn(v, s);
+    if (has_z) y = __fadd_rn(y, z);
+    return rintf(y);
+  }
+  return r;
+}
+
+template <typename T, int ROT>
+__global__ void __launch_bounds__(NT) rtn_fast_kernel(const RtnArgs a) {
+  constexpr int K = ROT == 256 ? 4 : (ROT == 64 ? 3 : 2);  // radix-4 stages
+  constexpr float DESCALE = ROT == 256 ? 0.0625f : (ROT == 64 ? 0.125f : 0.25f);
+  constexpr float UP = 1.f / DESCALE;
+  constexpr int TP = 16 * 16 + 16;  // transpose stride per 16-lane group (floats)
+  __shared__ __align__(16) float tr[(NT / 16) * TP];
+  __shared__ float red[32];
+  __shared__ double red_d[32];
+  const int64_t row = blockIdx.x;
+  const int ch = threadIdx.x;
+  const int64_t c0 = (int64_t)ch * 16;
+  const bool act = c0 < a.npad;
+  const bool has_z = a.asym != 0;
+  const float qmin = a.bits == 4 ? -8.f : -128.f;
+  const float qmax = a.bits == 4 ? 7.f : 127.f;
+
+  float v[16];
+  const T* src = reinterpret_cast<const T*>(a.W) + row * a.ldw + c0;
+  constexpr int V = 16 / sizeof(T);
+  if (act && c0 + 16 <= a.N && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 16 / V; ++q) {
+      const uint4 raw = reinterpret_cast<const uint4*>(src)[q];
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int u = 0; u < V; ++u) v[q * V + u] = load_as_f32(e + u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = (act && c0 + j < a.N) ? load_as_f32(src + j) : 0.f;
+  }
+  if (a.clamp > 0.f) {  // outlier sanitize; the select loop only when a weight exceeds the clamp
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(v[j]));
+    if (m > a.clamp) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = fabsf(v[j]) > a.clamp ? 0.f : v[j];
+    }
+  }
+  // ---- group Hadamard, scaled by 2^K ----
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4_unscaled(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4_unscaled(v[q], v[4 + q], v[8 + q], v[12 + q]);
+  const int lane16 = ch & 15;
+  float* trg = tr + (ch >> 4) * TP;
+  if (ROT == 64) cross4_unscaled(v, 1);
+  if (ROT == 256) {
+    // lane l (of the group's 16) holds in-group elements 16 l + j.  Transpose so
+    // that lane t holds elements 16 l' + t for l' = 0..15: its 16 values then
+    // span the two high digits.  Element (l, j) goes to row j of the group's
+    // tile at column chunk ((l >> 2) + (j >> 1)) & 3 (a skew that keeps both
+    // the scalar stores and the vector loads free of bank conflicts).
+    const int lq = lane16 >> 2, lr = lane16 & 3;
+    int off[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) off[k] = (((lq + k) & 3) << 2) + lr;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) trg[j * 16 + off[(j >> 1) & 3]] = v[j];
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float4 t = *reinterpret_cast<const float4*>(trg + lane16 * 16 + ((((c + (lane16 >> 1)) & 3)) << 2));
+      v[4 * c] = t.x;
+      v[4 * c + 1] = t.y;
+      v[4 * c + 2] = t.z;
+      v[4 * c + 3] = t.w;
+    }
+    // v[4c + u] = element (l' = 4c + u, j = lane16): digits l' & 3 (u) and l' >> 2 (c)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) h4_unscaled(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) h4_unscaled(v[u], v[4 + u], v[8 + u], v[12 + u]);
+  }
+  (void)K;
+
+  // ---- per-row scale (converter/scales.py), on the scaled values ----
+  float s = 0.f, zp = 0.f;
+  {
+    float amax = 0.f, wmin = __int_as_float(0x7f800000), wmax = __int_as_float(0xff800000);
+    if (act) {
+      if (has_z) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          wmin = min_nan(wmin, v[j]);
+          wmax = max_nan(wmax, v[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) amax = max_nan(amax, fabsf(v[j]));
+      }
+    }
+    if (has_z) {
+      wmin = __fmul_rn(cta_reduce(wmin, OpMin(), red), DESCALE);
+      wmax = __fmul_rn(cta_reduce(wmax, OpMax(), red), DESCALE);
+    } else {
+      amax = __fmul_rn(cta_reduce(amax, OpMax(), red), DESCALE);
+    }
+    const float div = has_z ? (qmax - qmin) : (a.bits == 4 ? 7.f : 127.f);
+    if (a.nratios == 0) {
+      if (has_z) {
+        s = clamp_scale(__fdiv_rn(__fsub_rn(wmax, wmin), div));
+        s = fix_asym(s, wmin, wmax, qmin, qmax);
+        zp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, s))), qmin, qmax);
+        if (a.zero_group_zp0 && wmin == 0.f && wmax == 0.f) zp = 0.f;
+      } else {
+        s = clamp_scale(__fdiv_rn(amax, div));
+      }
+    } else {
+      float best_mse = 0.f;
+      for (int r = 0; r < a.nratios; ++r) {
+        const float ratio = a.ratios[r];
+        float cs, czp = 0.f;
+        if (has_z) {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(__fsub_rn(wmax, wmin), ratio), div));
+          cs = fix_asym(cs, wmin, wmax, qmin, qmax);
+          czp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, cs))), qmin, qmax);
+        } else {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(amax, ratio), div));
+        }
+        const float csk = __fmul_rn(cs, UP), rcs = __frcp_rn(csk);
+        float part = 0.f;
+        if (act) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float q = clampf(fast_rint_div(v[j], csk, rcs, czp, has_z), qmin, qmax);
+            const float deq = has_z ? __fmul_rn(__fsub_rn(q, czp), csk) : __fmul_rn(q, csk);
+            const float e = __fsub_rn(v[j], deq);
+            part = __fadd_rn(part, __fmul_rn(e, e));
+          }
+        }
+        // the common 2^2K factor does not change which candidate wins
+        const float mse = __fdiv_rn(cta_reduce(part, OpSum(), red), (float)a.npad);
+        if (r == 0 || mse < best_mse) {
+          best_mse = mse;
+          s = cs;
+          zp = czp;
+        }
+      }
+    }
+  }
+  const uint16_t s16 = __half_as_ushort(__float2half_rn(s));
+  if (threadIdx.x == 0) {
+    if (a.scales) a.scales[row] = s16;
+    if (a.zp && a.asym) a.zp[row] = (int8_t)zp;
+  }
+
+  // ---- codes, verify statistics (scaled), packing ----
+  const float sk = __fmul_rn(__half2float(__ushort_as_half(s16)), UP);
+  const float rs = __frcp_rn(sk);
+  float part = 0.f, mx = 0.f;
+  uint32_t cb[4] = {0u, 0u, 0u, 0u};  // the 16 codes as bytes, in register order
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float q = clampf(fast_rhaz(v[j], sk, rs, zp, has_z), qmin, qmax);
+    const float deq = has_z ? __fmul_rn(__fsub_rn(q, zp), sk) : __fmul_rn(q, sk);
+    const float d = __fsub_rn(v[j], deq);
+    part = __fmaf_rn(d, d, part);
+    mx = max_nan(mx, fabsf(d));
+    cb[j >> 2] |= (small_int_bits(q) & 255u) << (8 * (j & 3));
+  }
+  if (ROT == 256) {
+    // back to row order: byte (l', j) of the group's 16 x 16 code tile
+    __syncwarp();
+    uint8_t* tb = reinterpret_cast<uint8_t*>(trg);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) tb[(4 * c + u) * 16 + lane16] = (uint8_t)(cb[c] >> (8 * u));
+    __syncwarp();
+    const uint4 t = *reinterpret_cast<const uint4*>(tb + lane16 * 16);
+    cb[0] = t.x;
+    cb[1] = t.y;
+    cb[2] = t.z;
+    cb[3] = t.w;
+  }
+  if (act) {
+    if (a.codes) {
+      int8_t* dst = a.codes + row * a.ldc + c0;
+      if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(cb[0], cb[1], cb[2], cb[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dst[j] = (int8_t)(cb[j >> 2] >> (8 * (j & 3)));
+      }
+    }
+    if (a.packed) {
+      uint32_t p2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        // bytes b0..b7 (two words) -> nibbles: (b0 & 15) | (b1 & 15) << 4 | ...
+        uint32_t x = cb[2 * h] & 0x0F0F0F0Fu, y = cb[2 * h + 1] & 0x0F0F0F0Fu;
+        x = (x | (x >> 4)) & 0x00FF00FFu;
+        y = (y | (y >> 4)) & 0x00FF00FFu;
+        p2[h] = __byte_perm(x, y, 0x6420);
+      }
+      uint8_t* dst = a.packed + row * a.ldp + c0 / 2;
+      if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(p2[0], p2[1]);
+      } else {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) dst[b] = (uint8_t)(p2[b >> 2] >> (8 * (b & 3)));
+      }
+    }
+  } else {
+    part = 0.f;
+    mx = 0.f;
+  }
+  if (a.row_sqerr || a.row_maxerr) {
+    double sq = warp_sum_d((double)part);
+    for (int o = 16; o; o >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+      red_d[threadIdx.x >> 5] = sq;
+      red[threadIdx.x >> 5] = mx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      float m = 0.f;
+      for (int w = 0; w < NT / 32; ++w) {
+        t += red_d[w];
+        m = nmax(m, red[w]);
+      }
+      if (a.row_sqerr) a.row_sqerr[row] = t * (double)DESCALE * (double)DESCALE;
+      if (a.row_maxerr) a.row_maxerr[row] = __fmul_rn(m, DESCALE);
+    }
+  }
+}
+
+template <int ROT>
+void launch_rtn_fast(const RtnArgs& a, int64_t M, cudaStream_t st) {
+  switch (a.dtype) {
+    case IC_F16: rtn_fast_kernel<__half, ROT><<<(unsigned)M, NT, 0, st>>>(a); break;
+    case IC_BF16: rtn_fast_kernel<__nv_bfloat16, ROT><<<(unsigned)M, NT, 0, st>>>(a); break;
+    default: rtn_fast_kernel<float, ROT><<<(unsigned)M, NT, 0, st>>>(a); break;
+  }
+}
+
 __global__ void pack_kernel(const int8_t* __restrict__ codes, int64_t M, int64_t K, int64_t ldc,
                             uint8_t* __restrict__ packed, int64_t ldp, unsigned* flags) {
   const int64_t kp = (K + 1) / 2;
@@ -478,9 +782,26 @@ __global__ void unpack_kernel(const uint8_t* __restrict__ packed, int64_t M, int
   }
 }
 
+// IC_RTN_FAST=0 selects the previous register kernel (A/B and parity checks)
+bool fast_off() {
+  static const bool off = [] {
+    const char* e = getenv("IC_RTN_FAST");
+    return e && e[0] == '0';
+  }();
+  return off;
+}
+
 int launch_rtn(RtnArgs& a, int64_t M, cudaStream_t st) {
   if (M == 0 || a.npad == 0) return IC_OK;
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rtn: too many rows");
+  if (a.G == 1 && !a.given && a.npad <= 16 * NT && a.npad % 16 == 0 && !fast_off() &&
+      (a.rot == 16 || a.rot == 64 || a.rot == 256)) {
+    if (a.rot == 256) launch_rtn_fast<256>(a, M, st);
+    else if (a.rot == 64) launch_rtn_fast<64>(a, M, st);
+    else launch_rtn_fast<16>(a, M, st);
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
   if (a.G == 1 && !a.given && a.npad <= 16 * NT && a.npad % 16 == 0 && (a.rot <= 1 || hadamard_regs_ok(a.rot))) {
     switch (a.dtype) {
       case IC_F16: rtn_regs_kernel<__half><<<(unsigned)M, NT, 0, st>>>(a); break;

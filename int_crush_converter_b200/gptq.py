@@ -340,6 +340,10 @@ def check_layer(res: dict) -> dict:
     status = int(res["stats"][2].item())
     if status & nat.DEV_NOT_PD:
         raise nat.NotPositiveDefinite("Hessian is not positive definite")
+    if status & nat.DEV_BAD_SCALE:  # pipeline.py:933-940 logs the same condition
+        import warnings
+        warnings.warn("Bad scales detected (a NaN weight row): scale NaN, zero-point and codes 0 for that row",
+                      stacklevel=2)
     return res
 
 

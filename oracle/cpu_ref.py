@@ -895,3 +895,43 @@ def compute_smoothing_factors(act_amax, W, alpha=0.5):  # smoothquant.py:11-52
     act = _c(np.asarray(act_amax, f32), SMOOTHQUANT_AMAX_FLOOR).astype(f32)
     ws = _c(np.abs(np.asarray(W, f32)).max(axis=0), SMOOTHQUANT_AMAX_FLOOR).astype(f32)
     return (torch.from_numpy(act).pow(alpha).numpy() / torch.from_numpy(ws).pow(1.0 - alpha).numpy()).astype(f32)
+
+
+# ---------------------------------------------------------------- PermuQuant
+def channel_second_moments(W):  # permuquant.py:13-22
+    return (np.asarray(W, f32) ** 2).mean(axis=0, dtype=np.float64).astype(f32)
+
+
+def permuquant_order(W, act_mu2=None, alpha=0.5):  # permuquant.py:25-67
+    """Channels by descending second moment (or joint key), ties by index."""
+    key = channel_second_moments(W)
+    if act_mu2 is not None:
+        import torch
+        a = torch.from_numpy(np.maximum(np.asarray(act_mu2, f32), f32(1e-12)))
+        w = torch.from_numpy(np.maximum(key, f32(1e-12)))
+        key = (a.pow(alpha) * w.pow(1.0 - alpha)).numpy()
+    return np.argsort(-key.astype(np.float64), kind="stable")
+
+
+def compute_group_quant_error(W, group_size=128, int_bits=4):  # permuquant.py:70-105
+    W = np.asarray(W, f32)
+    M, N = W.shape
+    if int_bits == 8:
+        s = calculate_scales_int8(W).astype(f32)
+        q = quantize_weights_int8(W, s)
+        dq = q.astype(f32) * s
+    else:
+        s = calculate_scales(W, group_size)
+        q = quantize_weights(W, s, group_size)
+        G = q.shape[1] // group_size
+        dq = (q.reshape(M, G, group_size).astype(f32) * s.astype(f32)[:, :, None]).reshape(M, -1)[:, :N]
+    return float(((W - dq).astype(np.float64) ** 2).sum())
+
+
+def find_permutation_with_acceptance(W, act_mu2=None, alpha=0.5, group_size=128, tau=0.0,
+                                     int_bits=4):  # permuquant.py:108-150
+    perm = permuquant_order(W, act_mu2, alpha)
+    e0 = compute_group_quant_error(W, group_size, int_bits)
+    e1 = compute_group_quant_error(np.asarray(W, f32)[:, perm], group_size, int_bits)
+    rel = (e0 - e1) / e0 if e0 > 0 else 0.0
+    return perm, bool(rel > tau), e0, e1

@@ -233,3 +233,41 @@ def sq_inputs(case: dict):
         hd = np.sqrt(hd).astype(f32) * f32(3.0)
     W[:, 5] = 0.0  # an all-zero weight column hits the weight floor
     return W, hd
+
+
+# PermuQuant (permuquant.py:13-211): candidate order, group errors, acceptance
+PQ_CASES = {
+    "pq_w_g128": dict(M=64, N=512, seed=141, group=128, bits=4, joint=False),
+    "pq_joint_g128": dict(M=64, N=512, seed=142, group=128, bits=4, joint=True),
+    "pq_w_rowwise": dict(M=64, N=512, seed=143, group=512, bits=4, joint=False),
+    "pq_w_int8": dict(M=48, N=384, seed=144, group=128, bits=8, joint=False),
+}
+
+
+def pq_inputs(case: dict):
+    """Weights whose channel magnitudes vary (so the order and the group
+    errors are far from ties) and activation second moments."""
+    M, N, seed = case["M"], case["N"], case["seed"]
+    rng = np.random.default_rng(seed)
+    colscale = np.exp(rng.normal(0.0, 1.0, N))
+    W = (rng.standard_normal((M, N)) * 0.02 * colscale).astype(np.float16).astype(f32)
+    act = (rng.lognormal(0.0, 1.0, N) ** 2).astype(f32) if case["joint"] else None
+    return W, act
+
+
+# SVD-absorbed split (svd.py:35-75): a planted low-rank part plus noise
+SVD_CASES = {
+    "svd_r16": dict(M=256, N=512, seed=151, rank=16, planted=16),
+    "svd_r32_wide": dict(M=192, N=640, seed=152, rank=32, planted=24),
+    "svd_r8_tall": dict(M=768, N=256, seed=153, rank=8, planted=12),
+}
+
+
+def svd_inputs(case: dict):
+    M, N, seed, k = case["M"], case["N"], case["seed"], case["planted"]
+    rng = np.random.default_rng(seed)
+    sv = np.geomspace(1.0, 0.05, k)
+    A = rng.standard_normal((M, k)) * sv
+    B = rng.standard_normal((k, N))
+    W = 0.02 * (A @ B) / np.sqrt(N) * 8 + 0.002 * rng.standard_normal((M, N))
+    return W.astype(np.float32)

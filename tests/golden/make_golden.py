@@ -188,6 +188,32 @@ def main() -> None:
         else:
             put(name, s=smoothquant.compute_smoothing_factors(T(hd), T(W), alpha=c["alpha"]))
 
+
+    from converter import permuquant
+    for name, c in C.PQ_CASES.items():
+        W, act = C.pq_inputs(c)
+        Wt = T(W)
+        at = None if act is None else T(act)
+        mu2 = permuquant.channel_second_moments(Wt)
+        if act is None:
+            perm = permuquant.find_permutation_weight(Wt, c["group"])
+        else:
+            perm = permuquant.find_permutation_joint(Wt, at, 0.5, c["group"])
+        e0 = permuquant.compute_group_quant_error(Wt, c["group"], c["bits"])
+        e1 = permuquant.compute_group_quant_error(Wt[:, perm], c["group"], c["bits"])
+        p2, acc = permuquant.find_permutation_with_acceptance(Wt, at, 0.5, c["group"], 0.0, c["bits"])
+        put(name, mu2=mu2, perm=perm, err=np.float64(e0), err_perm=np.float64(e1), accepted=np.array(bool(acc)),
+            chk=gi.checksum(W))
+
+
+    from converter import svd
+    for name, c in C.SVD_CASES.items():
+        W = C.svd_inputs(c)
+        torch.manual_seed(0)
+        r = svd.decompose_weight(T(W), rank=c["rank"])
+        put(name, res_energy=np.float64((r.residual.double() ** 2).sum().item()),
+            L1_shape=np.array(r.L1.shape), L2_shape=np.array(r.L2.shape), chk=gi.checksum(W))
+
     np.savez_compressed(args.out, **out)
     print(f"wrote {len(out)} arrays to {args.out} ({os.path.getsize(args.out)} bytes)")
 

@@ -195,3 +195,83 @@ def test_greedy_rows_cost_bound(golden, name):
         return np.einsum("ij,ij->i", E @ Hd, E)
     assert np.all(rowcost(out) <= rowcost(g) * (1 + 1e-3) + 1e-30)
     assert np.mean(out == g) > 0.99
+
+
+@pytest.mark.parametrize("name", list(C.PQ_CASES))
+def test_permuquant_on_device(golden, name):
+    """PermuQuant on the GPU against the reference: candidate order exact,
+    group errors within 1e-5 of the reference's fp32 sums, the acceptance
+    decision equal; with groups spanning the row the permuted error equals the
+    unpermuted one exactly (never accepted)."""
+    from int_crush_converter_b200 import permuquant as PQ
+    c = C.PQ_CASES[name]
+    W, act = C.pq_inputs(c)
+    Wt = cu(W).half()
+    at = None if act is None else cu(act)
+    np.testing.assert_allclose(np_(PQ.channel_second_moments(Wt)), golden[name + "/mu2"], rtol=2e-6)
+    perm, acc = PQ.find_permutation_with_acceptance(Wt, at, 0.5, c["group"], 0.0, c["bits"])
+    assert np.array_equal(np_(perm), golden[name + "/perm"])
+    assert acc == bool(golden[name + "/accepted"])
+    e0 = PQ.compute_group_quant_error(Wt, c["group"], c["bits"])
+    assert abs(e0 / float(golden[name + "/err"]) - 1) < 1e-5
+    e1 = PQ.compute_group_quant_error(PQ.apply_permutation_to_weight(Wt, perm), c["group"], c["bits"])
+    assert abs(e1 / float(golden[name + "/err_perm"]) - 1) < 1e-5
+    if c["group"] >= W.shape[1] or c["bits"] == 8:
+        assert PQ._errors(Wt.contiguous(), perm, c["group"], c["bits"]) == e0
+
+
+def test_fused_layer_nan_row_matches_pipeline_repair():
+    """A NaN weight: the pipeline's verify step sees a NaN scale and repairs the
+    row (pipeline.py:935-1007), which reproduces the NaN scale and sets the
+    row's zero-point and codes to 0 (torch's NaN -> int8).  The fused call gives
+    those outputs directly, flags the layer (status bit 8), reports the NaN
+    MSE the pipeline computes before repairing, and leaves every other row
+    bit-identical (GPTQ rows are independent given the Hessian)."""
+    from int_crush_converter_b200 import _native as nat
+    from tests.golden import inputs as gi
+    M, N = 64, 512
+    W = gi.weight_outlier_cols(31, M, N)
+    H = gi.hessian_lognormal(32, N, 2 * N)
+    Wn = W.copy()
+    Wn[3, 100] = np.nan
+    Wz = W.copy()
+    Wz[3] = 0.0
+    a = B.quantize_gptq_layer(cu(Wn), cu(H), rot_size=256, want_codes=True, check=False)
+    b = B.quantize_gptq_layer(cu(Wz), cu(H), rot_size=256, want_codes=True)
+    st = np_(a["stats"])
+    assert int(st[2]) & nat.DEV_BAD_SCALE and not int(st[2]) & nat.DEV_NOT_PD
+    assert np.isnan(st[0])
+    s = np_(a["scales"]).astype(np.float32)
+    assert np.isnan(s[3, 0]) and np.isfinite(np.delete(s, 3, axis=0)).all()
+    assert int(np_(a["zero_points"])[3, 0]) == 0
+    assert not np_(a["codes"])[3].any() and not np_(a["packed"])[3].any()
+    keep = np.arange(M) != 3
+    assert np.array_equal(np_(a["codes"])[keep], np_(b["codes"])[keep])
+    assert np.array_equal(np_(a["scales"])[keep], np_(b["scales"])[keep])
+    assert int(np_(b["stats"])[2]) == 0
+
+
+@pytest.mark.parametrize("name", list(C.SVD_CASES))
+def test_svd_absorbed_split(golden, name):
+    """decompose_weight on the GPU: the reference's shapes and dtypes, a residual
+    equal to W - L1 L2 (fp16 factors), and residual energy within 3% of the
+    reference's randomized split and within 5% of the optimal rank-r
+    truncation (numpy SVD) -- the two randomized runs draw different test
+    matrices, so the factors themselves are not comparable."""
+    from int_crush_converter_b200 import svd as S
+    c = C.SVD_CASES[name]
+    W = C.svd_inputs(c)
+    torch.manual_seed(0)
+    r = S.decompose_weight(cu(W), rank=c["rank"])
+    assert r.L1.dtype == torch.float16 and r.L2.dtype == torch.float16 and r.residual.dtype == torch.float32
+    assert tuple(r.L1.shape) == tuple(golden[name + "/L1_shape"]) and tuple(r.L2.shape) == tuple(golden[name + "/L2_shape"])
+    res = np_(r.residual).astype(np.float64)
+    recon = W.astype(np.float64) - np_(r.L1).astype(np.float64) @ np_(r.L2).astype(np.float64)
+    assert np.abs(res - recon).max() <= 1e-5 * np.abs(W).max()
+    e = float((res ** 2).sum())
+    sv = np.linalg.svd(W.astype(np.float64), compute_uv=False)
+    opt = float((sv[c["rank"]:] ** 2).sum())
+    assert e <= opt * 1.05, (e, opt)
+    assert abs(e / float(golden[name + "/res_energy"]) - 1) < 0.03
+    rc = S.decompose_weight(torch.from_numpy(W), rank=c["rank"])  # CPU tensors in, CPU out
+    assert rc.residual.device.type == "cpu" and rc.L1.device.type == "cpu"

@@ -185,3 +185,18 @@ def test_smoothing_factors_from_hessian_diag(golden, name):
     else:
         s = R.compute_smoothing_factors(hd, W, c["alpha"])
     assert np.array_equal(s, golden[name + "/s"])
+
+
+@pytest.mark.parametrize("name", list(C.PQ_CASES))
+def test_permuquant(golden, name):
+    """Order exact; errors within fp32-summation noise of the reference's; the
+    acceptance decision equal (these cases' improvements are far from 0, or
+    exactly 0 where the groups span the row)."""
+    c = C.PQ_CASES[name]
+    W, act = C.pq_inputs(c)
+    np.testing.assert_allclose(R.channel_second_moments(W), golden[name + "/mu2"], rtol=2e-6)
+    perm, acc, e0, e1 = R.find_permutation_with_acceptance(W, act, 0.5, c["group"], 0.0, c["bits"])
+    assert np.array_equal(perm, golden[name + "/perm"])
+    assert abs(e0 / float(golden[name + "/err"]) - 1) < 1e-5
+    assert abs(e1 / float(golden[name + "/err_perm"]) - 1) < 1e-5
+    assert acc == bool(golden[name + "/accepted"])
