@@ -40,6 +40,9 @@ struct GemmArgs {
   int chunk;  // k-tiles per TMEM accumulator chunk (3xTF32)
   int kofs;  // K index of column 0 of A/B in the full product (K-slab launches)
   int accum_in_place;  // D aliases C with beta == 1: a tile with K = 0 leaves D unchanged
+  int lower_rows;      // > 0: enumerate only the lower tiles of the first lower_rows tile rows,
+                       //      row by row from the top (square products with tri bit 0)
+  int row_major;       // tile order row by row from the top (tri bit 1: longest K first)
   int tri;  // bit 0: only output tiles on/below the diagonal (n0 <= m0);
             // bit 1: A rows are zero left of their own index (upper triangular
             //        A), so the K loop starts at the tile's first row m0
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(384, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int mt = (args.m + BM - 1) / BM, nt = (args.n + BN - 1) / BN;
-  const int ntiles = mt * nt;
+  const int ntiles = args.lower_rows > 0 ? args.lower_rows * (args.lower_rows + 1) / 2 : mt * nt;
 
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
@@ -343,7 +346,20 @@ __global__ void __launch_bounds__(384, 1)
   bool ok = true;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     int tm, tn;
-    tile_of(tile, mt, nt, args.group, tm, tn);
+    if (args.lower_rows > 0) {
+      // lower-triangle enumeration, row by row: rows near the top first, which
+      // for a triangular A (tri bit 1) are the tiles with the longest K
+      int r = (int)((sqrtf(8.f * (float)tile + 1.f) - 1.f) * 0.5f);
+      while ((r + 1) * (r + 2) / 2 <= tile) ++r;
+      while (r * (r + 1) / 2 > tile) --r;
+      tm = r;
+      tn = tile - r * (r + 1) / 2;
+    } else if (args.row_major) {
+      tm = tile / nt;
+      tn = tile - tm * nt;
+    } else {
+      tile_of(tile, mt, nt, args.group, tm, tn);
+    }
     const int m0 = tm * BM;
     const int n0 = tn * BN;
     if ((args.tri & 1) && n0 > m0) continue;  // strictly-upper tile of a symmetric/lower result
@@ -727,8 +743,10 @@ int launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, 
            const GemmArgs& a, cudaStream_t st) {
   using C = Cfg<BN, PASSES>;
   IC_TRY((prepare<BN, PASSES>()));
-  const int64_t tiles = cdiv(a.n, BN) * cdiv(a.m, BM);
+  const int64_t tiles = a.lower_rows > 0 ? (int64_t)a.lower_rows * (a.lower_rows + 1) / 2
+                                         : cdiv(a.n, BN) * cdiv(a.m, BM);
   if (tiles > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "gemm: too many tiles");
+  if (tiles == 0) return IC_OK;
   int ctas = 0;
   IC_TRY(persistent_ctas(&ctas));
   gemm_tn_kernel<BN, PASSES><<<(unsigned)std::min<int64_t>(tiles, ctas), 384, C::SMEM, st>>>(ah, al, bh, bl, a);
@@ -813,6 +831,16 @@ int tune_chunk() {
   return v;
 }
 
+// Tile orders for triangular products (IC_GEMM_TRI_ORDER=0 restores the
+// grouped order over all tiles, for A/B runs)
+bool tile_order_on() {
+  static const bool on = [] {
+    const char* e = getenv("IC_GEMM_TRI_ORDER");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, const float* a_lo,
               int64_t lda, const float* b_hi, const float* b_lo, int64_t ldb, float beta,
               const float* c_hi, const float* c_lo, int64_t ldc, float* d_hi, float* d_lo,
@@ -830,8 +858,18 @@ int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, c
   unsigned* flags = device_flags();
   if (!flags) return fail(IC_ERR_CUDA, "device status word unavailable");
   const int in_place = beta == 1.f && c_hi == d_hi && c_lo == d_lo && ldc == ldd;
+  const int64_t mt = cdiv(m, BM);
+  int lower_rows = 0;
+  if ((tri & 1) && m == n && tile_order_on()) {
+    lower_rows = (int)mt;
+    // accumulating a K-slab of a triangular A in place: tile rows starting at
+    // or below the slab's end get nothing from it and are not launched
+    if ((tri & 2) && in_place) lower_rows = (int)std::min<int64_t>(mt, cdiv(kofs + (k > 0 ? k : 0), BM));
+  }
+  const int row_major = (tri & 2) && lower_rows == 0 && tile_order_on();
   GemmArgs a{(int)m, (int)n, (int)(k > 0 ? k : 0), alpha, beta, c_hi, c_lo, (long long)ldc,
-             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tune_group(), tune_chunk(), kofs, in_place, tri};
+             d_hi, d_lo, (long long)ldd, flags, vec ? 1 : 0, tune_group(), tune_chunk(), kofs, in_place,
+             lower_rows, row_major, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
   if (passes == 3 && m > BM && pair_enabled()) {

@@ -747,6 +747,407 @@ __global__ void __launch_bounds__(NT) rtn_fast_kernel(const RtnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Paired fast path (rows of 1024 * k <= 4096 elements): each thread owns two
+// chunks of 16 elements that sit at the same position of two groups half a
+// row apart (columns 16t.. and npad/2 + 16t..), so every per-element operation
+// of the two chunks is the same instruction on different data: they run as
+// the sm_100 packed fp32 pair instructions (add/sub/mul/fma .f32x2, IEEE
+// round-to-nearest per lane like the scalar ones, so results stay
+// bit-identical), halving the instruction count of the butterflies, the
+// quotients, the rounding and the statistics.  One CTA of npad/32 threads per
+// row; otherwise the same algorithm as rtn_fast_kernel.
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 pk(float a, float b) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float lo_of(f2 r) { return __uint_as_float((uint32_t)(r & 0xffffffffull)); }
+__device__ __forceinline__ float hi_of(f2 r) { return __uint_as_float((uint32_t)(r >> 32)); }
+__device__ __forceinline__ uint32_t lo_of_bits(f2 r) { return (uint32_t)(r & 0xffffffffull); }
+__device__ __forceinline__ uint32_t hi_of_bits(f2 r) { return (uint32_t)(r >> 32); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 add2_rm(f2 a, f2 b) {
+  f2 d;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ void h4p(f2& x0, f2& x1, f2& x2, f2& x3) {
+  const f2 p = add2(x0, x1), m = sub2(x0, x1), P = add2(x2, x3), Mm = sub2(x2, x3);
+  x0 = add2(p, Mm);
+  x1 = sub2(p, Mm);
+  x2 = add2(m, P);
+  x3 = sub2(P, m);
+}
+__device__ __forceinline__ float clamp_nan(float x, float lo, float hi) { return min_nan(max_nan(x, lo), hi); }
+// y (pair) = corrected quotient v / s (+ z); per lane the IEEE division where
+// the rounding boundary is within 2^-14 (see fast_rhaz / fast_rint_div)
+__device__ __forceinline__ f2 quot2(f2 v, f2 s, f2 ns, f2 rs, f2 z, bool has_z) {
+  const f2 q0 = mul2(v, rs);
+  f2 y = fma2(fma2(q0, ns, v), rs, q0);
+  if (has_z) y = add2(y, z);
+  return y;
+}
+constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+
+template <typename T, int ROT>
+__global__ void __launch_bounds__(128) rtn_pair_kernel(const RtnArgs a) {
+  constexpr float DESCALE = ROT == 256 ? 0.0625f : (ROT == 64 ? 0.125f : 0.25f);
+  constexpr float UP = 1.f / DESCALE;
+  __shared__ __align__(16) f2 tr[(128 / 16) * 256];  // one 16 x 16 tile of pairs per 16-lane group
+  __shared__ float red[8];
+  __shared__ double red_d[8];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x, nt = blockDim.x;
+  const int64_t half = a.npad / 2;
+  const int64_t ca = (int64_t)t * 16, cb = half + ca;
+  const bool has_z = a.asym != 0;
+  const float qmin = a.bits == 4 ? -8.f : -128.f;
+  const float qmax = a.bits == 4 ? 7.f : 127.f;
+
+  f2 v[16];
+  {
+    float x[16], y[16];
+    const T* src = reinterpret_cast<const T*>(a.W) + row * a.ldw;
+    constexpr int V = 16 / sizeof(T);
+    const bool fa = ca + 16 <= a.N && (reinterpret_cast<uintptr_t>(src + ca) & 15) == 0;
+    const bool fb = cb + 16 <= a.N && (reinterpret_cast<uintptr_t>(src + cb) & 15) == 0;
+    if (fa) {
+#pragma unroll
+      for (int q = 0; q < 16 / V; ++q) {
+        const uint4 raw = reinterpret_cast<const uint4*>(src + ca)[q];
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int u = 0; u < V; ++u) x[q * V + u] = load_as_f32(e + u);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) x[j] = ca + j < a.N ? load_as_f32(src + ca + j) : 0.f;
+    }
+    if (fb) {
+#pragma unroll
+      for (int q = 0; q < 16 / V; ++q) {
+        const uint4 raw = reinterpret_cast<const uint4*>(src + cb)[q];
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int u = 0; u < V; ++u) y[q * V + u] = load_as_f32(e + u);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) y[j] = cb + j < a.N ? load_as_f32(src + cb + j) : 0.f;
+    }
+    if (a.clamp > 0.f) {
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) m = fmaxf(m, fmaxf(fabsf(x[j]), fabsf(y[j])));
+      if (m > a.clamp) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] = fabsf(x[j]) > a.clamp ? 0.f : x[j];
+          y[j] = fabsf(y[j]) > a.clamp ? 0.f : y[j];
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = pk(x[j], y[j]);
+  }
+  // ---- group Hadamard on the pairs, scaled by 2^K ----
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4p(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h4p(v[q], v[4 + q], v[8 + q], v[12 + q]);
+  const int lane16 = t & 15;
+  f2* trg = tr + (t >> 4) * 256;
+  if (ROT == 64) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const f2 a1 = __shfl_xor_sync(0xffffffffu, v[j], 1);
+      const f2 a2 = __shfl_xor_sync(0xffffffffu, v[j], 2);
+      const f2 a3 = __shfl_xor_sync(0xffffffffu, v[j], 3);
+      v[j] = add2(add2(v[j], a1), sub2(a2, a3));
+    }
+  }
+  if (ROT == 256) {
+    // as rtn_fast_kernel, with 8-byte elements: element (l, j) goes to row j,
+    // pair slot 2 * (((l >> 1) + j) & 7) + (l & 1); lane t then reads row t as
+    // eight 16-byte chunks starting at chunk t (a rotation that keeps each
+    // quarter-warp's 128-bit loads on distinct banks)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) trg[j * 16 + 2 * (((lane16 >> 1) + j) & 7) + (lane16 & 1)] = v[j];
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 w = *reinterpret_cast<const uint4*>(trg + lane16 * 16 + 2 * ((c + lane16) & 7));
+      // slot c' = (c + t) & 7 holds l' = 2c'' with c'' = (c' - t) & 7 = c
+      v[2 * c] = ((f2)w.y << 32) | w.x;
+      v[2 * c + 1] = ((f2)w.w << 32) | w.z;
+    }
+    // v[l'] = element (l', j = lane16): digits l' & 3 and l' >> 2
+#pragma unroll
+    for (int c = 0; c < 4; ++c) h4p(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) h4p(v[u], v[4 + u], v[8 + u], v[12 + u]);
+  }
+
+  // ---- per-row scale on the scaled values (both chunks belong to the row) ----
+  float s = 0.f, zp = 0.f;
+  {
+    const float div = has_z ? (qmax - qmin) : (a.bits == 4 ? 7.f : 127.f);
+    const int w = t >> 5, nw = nt >> 5;
+    float amax = 0.f, wmin = __int_as_float(0x7f800000), wmax = __int_as_float(0xff800000);
+    if (has_z) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        wmin = min_nan(wmin, min_nan(lo_of(v[j]), hi_of(v[j])));
+        wmax = max_nan(wmax, max_nan(lo_of(v[j]), hi_of(v[j])));
+      }
+      float r0, r1;
+      asm("redux.sync.min.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r0) : "f"(wmin));
+      asm("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r1) : "f"(wmax));
+      if ((t & 31) == 0) {
+        red[w] = r0;
+        red[4 + w] = r1;
+      }
+      __syncthreads();
+      wmin = red[0];
+      wmax = red[4];
+      for (int k = 1; k < nw; ++k) {
+        wmin = nmin(wmin, red[k]);
+        wmax = nmax(wmax, red[4 + k]);
+      }
+      wmin = __fmul_rn(wmin, DESCALE);
+      wmax = __fmul_rn(wmax, DESCALE);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) amax = max_nan(amax, max_nan(fabsf(lo_of(v[j])), fabsf(hi_of(v[j]))));
+      float r0;
+      asm("redux.sync.max.abs.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r0) : "f"(amax));
+      if ((t & 31) == 0) red[w] = r0;
+      __syncthreads();
+      amax = red[0];
+      for (int k = 1; k < nw; ++k) amax = nmax(amax, red[k]);
+      amax = __fmul_rn(amax, DESCALE);
+    }
+    if (a.nratios == 0) {
+      if (has_z) {
+        s = clamp_scale(__fdiv_rn(__fsub_rn(wmax, wmin), div));
+        s = fix_asym(s, wmin, wmax, qmin, qmax);
+        zp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, s))), qmin, qmax);
+        if (a.zero_group_zp0 && wmin == 0.f && wmax == 0.f) zp = 0.f;
+      } else {
+        s = clamp_scale(__fdiv_rn(amax, div));
+      }
+    } else {
+      float best_mse = 0.f;
+      for (int r = 0; r < a.nratios; ++r) {
+        const float ratio = a.ratios[r];
+        float cs, czp = 0.f;
+        if (has_z) {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(__fsub_rn(wmax, wmin), ratio), div));
+          cs = fix_asym(cs, wmin, wmax, qmin, qmax);
+          czp = clampf(__fsub_rn(qmin, rhaz(__fdiv_rn(wmin, cs))), qmin, qmax);
+        } else {
+          cs = clamp_scale(__fdiv_rn(__fmul_rn(amax, ratio), div));
+        }
+        const float csk = __fmul_rn(cs, UP), rcs = __frcp_rn(csk);
+        const f2 S = pk(csk, csk), NS = pk(-csk, -csk), RS = pk(rcs, rcs), Z = pk(czp, czp);
+        const f2 M2 = pk(MAGIC, MAGIC);
+        f2 part2 = 0ull;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const f2 y = quot2(v[j], S, NS, RS, Z, has_z);
+          f2 rq = sub2(add2(y, M2), M2);  // round-half-even, |y| < 2^22
+          const float y0 = lo_of(y), y1 = hi_of(y);
+          float r0 = lo_of(rq), r1 = hi_of(rq);
+          if (!(fabsf(__fsub_rn(y0, r0)) <= 0.5f - 0x1p-14f) || !(fabsf(y0) < 4194304.f)) {
+            float e = __fdiv_rn(lo_of(v[j]), csk);
+            if (has_z) e = __fadd_rn(e, czp);
+            r0 = rintf(e);
+          }
+          if (!(fabsf(__fsub_rn(y1, r1)) <= 0.5f - 0x1p-14f) || !(fabsf(y1) < 4194304.f)) {
+            float e = __fdiv_rn(hi_of(v[j]), csk);
+            if (has_z) e = __fadd_rn(e, czp);
+            r1 = rintf(e);
+          }
+          const f2 q = pk(clamp_nan(r0, qmin, qmax), clamp_nan(r1, qmin, qmax));
+          const f2 deq = has_z ? mul2(sub2(q, Z), S) : mul2(q, S);
+          const f2 e = sub2(v[j], deq);
+          part2 = add2(part2, mul2(e, e));
+        }
+        // the same fp32 sum as rtn_fast_kernel: a chunk's 16 terms in order, a
+        // warp's chunks by an xor tree, then the warps in order -- chunk-a warps
+        // first (columns [0, npad/2)), then chunk-b warps
+        float tot;
+        {
+          f2 x = part2;
+          for (int o = 16; o; o >>= 1) x = add2(x, __shfl_xor_sync(0xffffffffu, x, o));
+          const int nw = nt >> 5;
+          __syncthreads();
+          if ((t & 31) == 0) {
+            red[t >> 5] = lo_of(x);
+            red[nw + (t >> 5)] = hi_of(x);
+          }
+          __syncthreads();
+          tot = red[0];
+          for (int k = 1; k < 2 * nw; ++k) tot = __fadd_rn(tot, red[k]);
+        }
+        const float mse = __fdiv_rn(tot, (float)a.npad);
+        if (r == 0 || mse < best_mse) {
+          best_mse = mse;
+          s = cs;
+          zp = czp;
+        }
+      }
+    }
+  }
+  const uint16_t s16 = __half_as_ushort(__float2half_rn(s));
+  if (t == 0) {
+    if (a.scales) a.scales[row] = s16;
+    if (a.zp && a.asym) a.zp[row] = (int8_t)zp;
+  }
+
+  // ---- codes, statistics, packing ----
+  const float sk = __fmul_rn(__half2float(__ushort_as_half(s16)), UP);
+  const float rsk = __frcp_rn(sk);
+  const f2 S = pk(sk, sk), NS = pk(-sk, -sk), RS = pk(rsk, rsk), Z = pk(zp, zp);
+  const f2 HALF = pk(0.5f, 0.5f), M2 = pk(MAGIC, MAGIC);
+  f2 part2 = 0ull;
+  float mx = 0.f;
+  uint32_t ca4[4] = {0u, 0u, 0u, 0u}, cb4[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const f2 y = quot2(v[j], S, NS, RS, Z, has_z);
+    const f2 ay = pk(fabsf(lo_of(y)), fabsf(hi_of(y)));
+    const f2 tt = add2(ay, HALF);
+    const f2 fl = sub2(add2_rm(tt, M2), M2);  // floor(|y| + 1/2)
+    const f2 d = sub2(tt, fl);
+    float q0 = copysignf(lo_of(fl), lo_of(y)), q1 = copysignf(hi_of(fl), hi_of(y));
+    if (fabsf(__fsub_rn(lo_of(d), 0.5f)) > 0.5f - 0x1p-14f || !(lo_of(tt) < 4194304.f)) {
+      float e = __fdiv_rn(lo_of(v[j]), sk);
+      if (has_z) e = __fadd_rn(e, zp);
+      q0 = rhaz(e);
+    }
+    if (fabsf(__fsub_rn(hi_of(d), 0.5f)) > 0.5f - 0x1p-14f || !(hi_of(tt) < 4194304.f)) {
+      float e = __fdiv_rn(hi_of(v[j]), sk);
+      if (has_z) e = __fadd_rn(e, zp);
+      q1 = rhaz(e);
+    }
+    const f2 q = pk(clamp_nan(q0, qmin, qmax), clamp_nan(q1, qmin, qmax));
+    const f2 deq = has_z ? mul2(sub2(q, Z), S) : mul2(q, S);
+    const f2 e = sub2(v[j], deq);
+    part2 = fma2(e, e, part2);
+    mx = max_nan(mx, max_nan(fabsf(lo_of(e)), fabsf(hi_of(e))));
+    const f2 bits = add2(q, M2);  // low byte = two's-complement code
+    ca4[j >> 2] |= ((uint32_t)lo_of_bits(bits) & 255u) << (8 * (j & 3));
+    cb4[j >> 2] |= ((uint32_t)hi_of_bits(bits) & 255u) << (8 * (j & 3));
+  }
+  if (ROT == 256) {
+    // codes back to row order through a 16 x 16 tile of 16-bit (chunk a, chunk b) pairs
+    __syncwarp();
+    uint16_t* tb = reinterpret_cast<uint16_t*>(trg);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        tb[(4 * c + u) * 16 + lane16] =
+            (uint16_t)(((ca4[c] >> (8 * u)) & 255u) | (((cb4[c] >> (8 * u)) & 255u) << 8));
+    __syncwarp();
+    const uint4 w0 = *reinterpret_cast<const uint4*>(tb + lane16 * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(tb + lane16 * 16 + 8);
+    const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      ca4[k] = __byte_perm(wd[2 * k], wd[2 * k + 1], 0x6420);
+      cb4[k] = __byte_perm(wd[2 * k], wd[2 * k + 1], 0x7531);
+    }
+  }
+  const int64_t cols[2] = {ca, cb};
+  const uint32_t* cw[2] = {ca4, cb4};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t* c4 = cw[h];
+    if (a.codes) {
+      int8_t* dst = a.codes + row * a.ldc + cols[h];
+      if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(c4[0], c4[1], c4[2], c4[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dst[j] = (int8_t)(c4[j >> 2] >> (8 * (j & 3)));
+      }
+    }
+    if (a.packed) {
+      uint32_t p2[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        uint32_t x = c4[2 * k] & 0x0F0F0F0Fu, y = c4[2 * k + 1] & 0x0F0F0F0Fu;
+        x = (x | (x >> 4)) & 0x00FF00FFu;
+        y = (y | (y >> 4)) & 0x00FF00FFu;
+        p2[k] = __byte_perm(x, y, 0x6420);
+      }
+      uint8_t* dst = a.packed + row * a.ldp + cols[h] / 2;
+      if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(p2[0], p2[1]);
+      } else {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) dst[b] = (uint8_t)(p2[b >> 2] >> (8 * (b & 3)));
+      }
+    }
+  }
+  if (a.row_sqerr || a.row_maxerr) {
+    // as rtn_fast_kernel: a chunk's 16 squared errors in fp32, chunks of a warp
+    // by an fp64 xor tree, warps in order (chunk-a warps first)
+    const double sa = warp_sum_d((double)lo_of(part2)), sb = warp_sum_d((double)hi_of(part2));
+    float m;
+    asm("redux.sync.max.abs.NaN.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(mx));
+    const int nw = nt >> 5;
+    __syncthreads();
+    if ((t & 31) == 0) {
+      red_d[t >> 5] = sa;
+      red_d[nw + (t >> 5)] = sb;
+      red[t >> 5] = m;
+    }
+    __syncthreads();
+    if (t == 0) {
+      double tt = 0.0;
+      float mm = 0.f;
+      for (int k = 0; k < 2 * nw; ++k) tt += red_d[k];
+      for (int k = 0; k < nw; ++k) mm = nmax(mm, red[k]);
+      if (a.row_sqerr) a.row_sqerr[row] = tt * (double)DESCALE * (double)DESCALE;
+      if (a.row_maxerr) a.row_maxerr[row] = __fmul_rn(mm, DESCALE);
+    }
+  }
+}
+
+template <int ROT>
+void launch_rtn_pair(const RtnArgs& a, int64_t M, cudaStream_t st) {
+  const unsigned threads = (unsigned)(a.npad / 32);
+  switch (a.dtype) {
+    case IC_F16: rtn_pair_kernel<__half, ROT><<<(unsigned)M, threads, 0, st>>>(a); break;
+    case IC_BF16: rtn_pair_kernel<__nv_bfloat16, ROT><<<(unsigned)M, threads, 0, st>>>(a); break;
+    default: rtn_pair_kernel<float, ROT><<<(unsigned)M, threads, 0, st>>>(a); break;
+  }
+}
+
 template <int ROT>
 void launch_rtn_fast(const RtnArgs& a, int64_t M, cudaStream_t st) {
   switch (a.dtype) {
@@ -791,9 +1192,26 @@ bool fast_off() {
   return off;
 }
 
+// IC_RTN_FAST=1 selects rtn_fast_kernel over the paired kernel (A/B checks)
+bool pair_on() {
+  static const bool on = [] {
+    const char* e = getenv("IC_RTN_FAST");
+    return !(e && (e[0] == '0' || e[0] == '1'));
+  }();
+  return on;
+}
+
 int launch_rtn(RtnArgs& a, int64_t M, cudaStream_t st) {
   if (M == 0 || a.npad == 0) return IC_OK;
   if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "rtn: too many rows");
+  if (a.G == 1 && !a.given && a.npad <= 4096 && a.npad % 1024 == 0 && pair_on() &&
+      (a.rot == 16 || a.rot == 64 || a.rot == 256)) {
+    if (a.rot == 256) launch_rtn_pair<256>(a, M, st);
+    else if (a.rot == 64) launch_rtn_pair<64>(a, M, st);
+    else launch_rtn_pair<16>(a, M, st);
+    IC_CHECK_LAUNCH();
+    return IC_OK;
+  }
   if (a.G == 1 && !a.given && a.npad <= 16 * NT && a.npad % 16 == 0 && !fast_off() &&
       (a.rot == 16 || a.rot == 64 || a.rot == 256)) {
     if (a.rot == 256) launch_rtn_fast<256>(a, M, st);

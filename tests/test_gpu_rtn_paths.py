@@ -1,9 +1,11 @@
-"""The fast fused-RTN kernel (one scale per row, rot 16 / 64 / 256, deferred
-Hadamard scaling, shared-memory transpose) against the previous register
-kernel (selected with IC_RTN_FAST=0 in a child process): codes, packed bytes,
-scales, zero-points and verify statistics must be bit-identical on every mode
-(INT4/INT8, symmetric/asymmetric, clipping-ratio search, padding, outliers
-above the sanitize clamp, NaN rows, fp16/bf16/fp32 inputs)."""
+"""The fused-RTN kernels against each other, each selected in a child process
+with IC_RTN_FAST: the paired kernel (default; two chunks per thread on the
+packed fp32 pair instructions), the fast kernel (=1; one scale per row,
+rot 16 / 64 / 256, deferred Hadamard scaling, shared-memory transpose) and the
+register kernel (=0).  Codes, packed bytes, scales, zero-points and verify
+statistics must be bit-identical on every mode (INT4/INT8,
+symmetric/asymmetric, clipping-ratio search, padding, outliers above the
+sanitize clamp, NaN rows, fp16/bf16/fp32 inputs)."""
 
 import os
 import subprocess
@@ -27,6 +29,9 @@ CASES = [
     (40, 200, 64, 4, False, None, "half"),
     (40, 512, 16, 8, True, None, "float"),
     (16, 4096, 16, 4, True, RATIOS, "half"),
+    (48, 3072, 64, 8, False, RATIOS, "bfloat16"),
+    (24, 2048, 256, 4, False, RATIOS, "half"),
+    (24, 1024, 64, 8, True, None, "float"),
 ]
 
 CHILD = r"""
@@ -54,16 +59,20 @@ np.savez({path!r}, **out)
 """
 
 
-def _run(fast: bool, path: str):
-    env = dict(os.environ, IC_RTN_FAST="1" if fast else "0")
+def _run(mode: str, path: str):
+    env = dict(os.environ)
+    env.pop("IC_RTN_FAST", None)
+    if mode:
+        env["IC_RTN_FAST"] = mode
     code = CHILD.format(root=ROOT, cases=CASES, path=path)
     subprocess.run([sys.executable, "-c", code], env=env, check=True, cwd=ROOT)
     return np.load(path)
 
 
-def test_fast_rtn_kernel_bit_identical_to_register_kernel(tmp_path):
-    a = _run(True, str(tmp_path / "fast.npz"))
-    b = _run(False, str(tmp_path / "regs.npz"))
+@pytest.mark.parametrize("mode", ["", "1"])
+def test_rtn_kernels_bit_identical_to_register_kernel(tmp_path, mode):
+    a = _run(mode, str(tmp_path / "a.npz"))
+    b = _run("0", str(tmp_path / "regs.npz"))
     assert sorted(a.files) == sorted(b.files)
     for k in a.files:
         x, y = a[k], b[k]
