@@ -620,7 +620,7 @@ def run_hbm_kernels(reps: int = 5) -> None:
             nat.check(lib.ic_rtn_fused(W.data_ptr(), nat.IC_F16, 4096, 4096, 4096, 256, 4, 0, None, 0, None,
                                        packed.data_ptr(), sc.data_ptr(), None, sq.data_ptr(), mx.data_ptr(), st))
     ms, gbs, frac = timed(rtn, 8 * (4096 * 4096 * 2.5 + 4096 * 2))
-    out.append(dict(kernel="rtn_fast_kernel<half,256> (ic_rtn_fused)", workload="config 1: 8 x fp16 [4096,4096] INT4 sym rot256",
+    out.append(dict(kernel="rtn_pair_kernel<half,256> (ic_rtn_fused)", workload="config 1: 8 x fp16 [4096,4096] INT4 sym rot256",
                     ms_per_call=ms, achieved_gbs=gbs, frac=frac))
     del Ws
     # config 2: RTN INT8 sym rot64 with the 5-ratio clip search, 16 x [3072,3072] + 16 x [12288,3072]
@@ -638,7 +638,7 @@ def run_hbm_kernels(reps: int = 5) -> None:
             nat.check(lib.ic_rtn_fused(W.data_ptr(), nat.IC_F16, m, 3072, 3072, 64, 8, 0, ratios, 5, c2.data_ptr(),
                                        None, sc2.data_ptr(), None, sq2.data_ptr(), mx2.data_ptr(), st))
     ms, gbs, frac = timed(rtn8, p2 * 3 + sum(W.shape[0] for W in W2) * 2)
-    out.append(dict(kernel="rtn_fast_kernel<half,64> (ic_rtn_fused)",
+    out.append(dict(kernel="rtn_pair_kernel<half,64> (ic_rtn_fused)",
                     workload="config 2: 16 x [3072,3072] + 16 x [12288,3072] fp16, INT8 sym rot64, 5 clipping ratios",
                     ms_per_call=ms, achieved_gbs=gbs, frac=frac))
     del W2, c2
