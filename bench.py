@@ -438,6 +438,13 @@ def run_device(args, rank: int, world: int) -> None:
     peak_s = bf16_s / 2.0 / 3.0
     cpu = reference_cpu_subprocess(1, 0, 0.0, "proj")
     dropin = run_dropin(dev) if args.dropin else None
+    other = None
+    if args.other_configs:
+        torch.cuda.empty_cache()
+        cpu_cfg = {c["config"]: c for c in reference_configs_subprocess()}
+        other = measure_configs(dev, _peaks().get("hbm_gbs"))
+        for d in other:
+            d["cpu_baseline"] = cpu_cfg.get(d["config"])
     ms_step = ms_max / args.steps
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "Mparams/s", "n_gpus": world, "steps": args.steps,
@@ -450,6 +457,7 @@ def run_device(args, rank: int, world: int) -> None:
                        model_sets=args.model_sets, params=n_params, order=args.order),
         "e2e": e2e,
         "dropin_e2e": dropin,
+        "other_configs": other,
         "gpu_launches": launches,
         "inverse_graphs_instantiated_in_timed_region": int(graphs),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
@@ -667,13 +675,14 @@ def run_hbm_kernels(reps: int = 5) -> None:
         print(json.dumps(o), flush=True)
 
 
-def run_configs() -> None:
+def measure_configs(dev: torch.device, peak_gbs: float | None = None, e2e: bool = True) -> list[dict]:
     """The BASELINE configs other than the headline one, each through the public
-    API on device-resident synthetic inputs of the config's shapes (seeded),
-    timed with CUDA events after a warm-up; one JSON line per config."""
+    API on synthetic inputs of the config's shapes (seeded), timed with CUDA
+    events after a warm-up: device-resident `value`; for the RTN configs the
+    HBM roofline (algorithmic bytes: fp16 in, codes out, fp16 scales) and an
+    `e2e` with the fp16 weights copied from pinned host memory and the codes
+    and scales copied back inside the timed region."""
     import int_crush_converter_b200 as B
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(21)
 
     def timed(fn, reps):
@@ -695,11 +704,37 @@ def run_configs() -> None:
             W[:, cols] *= outlier_mult
         return W.half()
 
+    def rtn_e2e(Ws, rot, bits, ratios, reps=2):
+        host = [W.cpu().pin_memory() for W in Ws]
+        outs = []
+        for W in Ws:
+            m, n = W.shape
+            outs.append((torch.empty(m, n // 2 if bits == 4 else n, dtype=torch.uint8 if bits == 4 else torch.int8)
+                         .pin_memory(), torch.empty(m, 1, dtype=torch.float16).pin_memory()))
+
+        def go():
+            for Wh, (c, sc) in zip(host, outs):
+                o = B.rtn_quantize_fused(Wh.to(dev, non_blocking=True), rot, int_bits=bits, clipping_ratios=ratios,
+                                         want_codes=bits == 8, want_packed=bits == 4)
+                c.copy_(o["packed"] if bits == 4 else o["codes"], non_blocking=True)
+                sc.copy_(o["scales"], non_blocking=True)
+        ms = timed(go, reps)
+        h2d = sum(W.numel() * 2 for W in Ws)
+        d2h = sum(c.numel() + sc.numel() * 2 for c, sc in outs)
+        return ms, h2d, d2h
+
     lines = []
     # config 1: RTN INT4 sym rot256, 8 x [4096,4096]
     W1 = [weights(4096, 4096, 0.02, 0.001, 20.0) for _ in range(8)]
-    ms = timed(lambda: [B.rtn_quantize_fused(W, 256, int_bits=4, want_codes=False) for W in W1], 3)
-    lines.append(dict(config=1, workload="RTN INT4 sym rot256, 8 fp16 layers [4096,4096]", params=8 * 4096 * 4096, ms=ms))
+    p1 = 8 * 4096 * 4096
+    ms = timed(lambda: [B.rtn_quantize_fused(W, 256, int_bits=4, want_codes=False) for W in W1], 5)
+    d = dict(config=1, workload="RTN INT4 sym rot256, 8 fp16 layers [4096,4096] (0.1% columns x20)", params=p1,
+             ms=ms, algorithmic_bytes=p1 * 2.5 + 8 * 4096 * 2)
+    if e2e:
+        ems, h2d, d2h = rtn_e2e(W1, 256, 4, None)
+        d["e2e"] = {"value": round(p1 / (ems * 1e-3) / 1e6, 2), "unit": "Mparams/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h}
+    lines.append(d)
     del W1
     # config 2: RTN INT8 sym rot64 with the clipping-ratio search, 16 x [3072,3072] + 16 x [12288,3072]
     t = torch.distributions.StudentT(torch.tensor(3.0, device=dev))
@@ -711,17 +746,23 @@ def run_configs() -> None:
         return W.half()
     W2 = [w2(3072, 3072) for _ in range(16)] + [w2(12288, 3072) for _ in range(16)]
     ratios = [0.8, 0.85, 0.9, 0.95, 1.0]
+    p2 = 16 * 3072 * 3072 + 16 * 12288 * 3072
     ms = timed(lambda: [B.rtn_quantize_fused(W, 64, int_bits=8, clipping_ratios=ratios, want_codes=True,
-                                             want_packed=False) for W in W2], 2)
-    lines.append(dict(config=2, workload="RTN INT8 sym rot64, clipping ratios {0.8..1.0}, 16 x [3072,3072] + "
-                      "16 x [12288,3072] fp16 (N(0,0.02^2) + Student-t(3) tails on 1%)",
-                      params=16 * 3072 * 3072 + 16 * 12288 * 3072, ms=ms))
+                                             want_packed=False) for W in W2], 3)
+    d = dict(config=2, workload="RTN INT8 sym rot64, clipping ratios {0.8..1.0}, 16 x [3072,3072] + "
+                                "16 x [12288,3072] fp16 (N(0,0.02^2) + Student-t(3) tails on 1%)",
+             params=p2, ms=ms, algorithmic_bytes=p2 * 3 + (16 * 3072 + 16 * 12288) * 2)
+    if e2e:
+        ems, h2d, d2h = rtn_e2e(W2, 64, 8, ratios)
+        d["e2e"] = {"value": round(p2 / (ems * 1e-3) / 1e6, 2), "unit": "Mparams/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h}
+    lines.append(d)
     del W2
     # config 4: LDLQ INT4 rot256, 2 iterations, 8 greedy passes, weight-only Hessian; one [8192,8192] layer
     W4 = weights(8192, 8192, 0.015, 0.0005, 30.0)
 
     def ldlq():
-        Wr = B.rotate_weights(W4, 256)
+        Wr = B.rotate_weights(W4.float(), 256)
         return B.ldlq_quantize_layer(Wr, None, block_size=128, int_bits=4, iterations=2, greedy_passes=8)
     import warnings
     with warnings.catch_warnings():
@@ -732,7 +773,100 @@ def run_configs() -> None:
     for d in lines:
         d.update(metric="Mparams quantized/s", value=round(d["params"] / (d["ms"] * 1e-3) / 1e6, 2),
                  ms=round(d["ms"], 3), data="synthetic, device-resident")
+        if "algorithmic_bytes" in d and peak_gbs:
+            gbs = d["algorithmic_bytes"] / (d["ms"] * 1e-3) / 1e9
+            d["roofline"] = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak_gbs, "unit": "GB/s",
+                             "frac": round(gbs / peak_gbs, 4), "traffic": None,
+                             "kernel": "rtn_pair_kernel (ic_rtn_fused), all layers of the config"}
+    return lines
+
+
+def reference_cpu_configs() -> list[dict]:
+    """The reference's own CPU code on bounded samples of configs 1, 2 and 4
+    (run with no GPU visible): one layer of each RTN config, and LDLQ with the
+    config's settings on a [1024, 1024] layer (the full [8192, 8192] greedy
+    search takes hours on the CPU)."""
+    import numpy as np
+    ref = _reference_converter()
+    if ref is None:
+        return []
+    import importlib
+    scales = importlib.import_module("converter.scales")
+    ldlq = importlib.import_module("converter.ldlq")
+    torch.set_num_threads(cpu_cores())
+    g = torch.Generator().manual_seed(3)
+    out = []
+
+    def run(fn, reps=2):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    W = (torch.randn(4096, 4096, generator=g) * 0.02).half().float()
+
+    def c1():
+        Wr = ref["rotation"].rotate_weights(W, 256)
+        s = scales.calculate_scales(Wr, Wr.shape[1])
+        ref["packing"].pack_int4(scales.quantize_weights(Wr, s, Wr.shape[1]))
+    sec = run(c1)
+    out.append(dict(config=1, value=round(4096 * 4096 / sec / 1e6, 3), unit="Mparams/s", cores=torch.get_num_threads(),
+                    kind="reference", sample="one [4096,4096] layer: rotate_weights -> calculate_scales -> "
+                                             "quantize_weights -> pack_int4"))
+    W = (torch.randn(3072, 3072, generator=g) * 0.02).half().float()
+    ratios = [0.8, 0.85, 0.9, 0.95, 1.0]
+
+    def c2():
+        Wr = ref["rotation"].rotate_weights(W, 64)
+        s = scales.calculate_scales_int8(Wr, clipping_ratios=ratios)
+        scales.quantize_weights_int8(Wr, s)
+    sec = run(c2)
+    out.append(dict(config=2, value=round(3072 * 3072 / sec / 1e6, 3), unit="Mparams/s", cores=torch.get_num_threads(),
+                    kind="reference", sample="one [3072,3072] layer: rotate_weights(64) -> calculate_scales_int8 "
+                                             "(5 ratios) -> quantize_weights_int8"))
+    W = (torch.randn(1024, 1024, generator=g) * 0.015).half().float()
+    import warnings
+
+    def c4():
+        Wr = ref["rotation"].rotate_weights(W, 256)
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            ldlq.ldlq_quantize_layer(Wr, None, block_size=128, int_bits=4, iterations=2, greedy_passes=8)
+    sec = run(c4, 1)
+    out.append(dict(config=4, value=round(1024 * 1024 / sec / 1e6, 3), unit="Mparams/s", cores=torch.get_num_threads(),
+                    kind="reference", sample="one [1024,1024] layer (the config's [8192,8192] takes hours): "
+                                             "LDLQ INT4 rot256, 2 iterations, 8 greedy passes"))
+    del np
+    return out
+
+
+def run_configs() -> None:
+    """Configs 1, 2 and 4 (one JSON line each), with the reference's CPU samples."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak = _peaks().get("hbm_gbs")
+    cpu = {c["config"]: c for c in reference_configs_subprocess()}
+    for d in measure_configs(dev, peak):
+        d["cpu_baseline"] = cpu.get(d["config"])
         print(json.dumps(d), flush=True)
+
+
+def _peaks() -> dict:
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def reference_configs_subprocess() -> list[dict]:
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE"):
+        env.pop(k, None)
+    p = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference-cpu-configs"], env=env,
+                       stdout=subprocess.PIPE, text=True)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("[")]
+    return json.loads(lines[-1]) if p.returncode == 0 and lines else []
 
 
 def main() -> None:
@@ -740,13 +874,15 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cpu"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cpu", "reference-cpu-configs"])
     ap.add_argument("--sets", type=int, default=8, help="distinct resident input sets per GPU (cycled)")
     ap.add_argument("--host-sets", type=int, default=2, help="distinct pinned host input sets per GPU (e2e)")
     ap.add_argument("--model-sets", type=int, default=MODEL_SETS, help="linear sets in the model (config 5: 40)")
     ap.add_argument("--order", default="lpt", choices=["lpt", "natural"], help="work-queue order of the layers")
     ap.add_argument("--depth", type=int, default=6, help="layers a rank keeps unfinished on its GPU")
     ap.add_argument("--dropin", type=int, default=1, help="also time the reference call shape (drop-in API)")
+    ap.add_argument("--other-configs", type=int, default=1,
+                    help="also measure configs 1, 2 and 4 (rank 0) with the reference's CPU samples")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--ref-sample", default="set", choices=["set", "proj"],
                     help="reference CPU arm: time whole sets or the proj layer only")
@@ -806,6 +942,9 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference-cpu":
         run_reference_cpu(args)
+        return
+    if args.impl == "reference-cpu-configs":
+        print(json.dumps(reference_cpu_configs()), flush=True)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
