@@ -976,15 +976,18 @@ __global__ void __launch_bounds__(128) rtn_pair_kernel(const RtnArgs a) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const f2 y = quot2(v[j], S, NS, RS, Z, has_z);
-          f2 rq = sub2(add2(y, M2), M2);  // round-half-even, |y| < 2^22
-          const float y0 = lo_of(y), y1 = hi_of(y);
+          // round-half-even by the magic add (|y| stays far below 2^22 here:
+          // |v| <= the row's absmax and cs >= absmax * 0.8 / 127 up to the
+          // scale clamp; a NaN fails the test below and takes the exact path)
+          f2 rq = sub2(add2(y, M2), M2);
+          const f2 dy = sub2(y, rq);
           float r0 = lo_of(rq), r1 = hi_of(rq);
-          if (!(fabsf(__fsub_rn(y0, r0)) <= 0.5f - 0x1p-14f) || !(fabsf(y0) < 4194304.f)) {
+          if (!(fabsf(lo_of(dy)) <= 0.5f - 0x1p-14f)) {
             float e = __fdiv_rn(lo_of(v[j]), csk);
             if (has_z) e = __fadd_rn(e, czp);
             r0 = rintf(e);
           }
-          if (!(fabsf(__fsub_rn(y1, r1)) <= 0.5f - 0x1p-14f) || !(fabsf(y1) < 4194304.f)) {
+          if (!(fabsf(hi_of(dy)) <= 0.5f - 0x1p-14f)) {
             float e = __fdiv_rn(hi_of(v[j]), csk);
             if (has_z) e = __fadd_rn(e, czp);
             r1 = rintf(e);
@@ -1042,12 +1045,16 @@ __global__ void __launch_bounds__(128) rtn_pair_kernel(const RtnArgs a) {
     const f2 fl = sub2(add2_rm(tt, M2), M2);  // floor(|y| + 1/2)
     const f2 d = sub2(tt, fl);
     float q0 = copysignf(lo_of(fl), lo_of(y)), q1 = copysignf(hi_of(fl), hi_of(y));
-    if (fabsf(__fsub_rn(lo_of(d), 0.5f)) > 0.5f - 0x1p-14f || !(lo_of(tt) < 4194304.f)) {
+    // |y| + 1/2 near an integer (d near 0 or 1): the exact division decides.
+    // |y| is bounded by the scale (|v| <= absmax, s >= absmax / 7.x, or the
+    // asymmetric range); a NaN passes the test and stays NaN as rhaz(NaN).
+    const f2 dh = sub2(d, HALF);
+    if (fabsf(lo_of(dh)) > 0.5f - 0x1p-14f) {
       float e = __fdiv_rn(lo_of(v[j]), sk);
       if (has_z) e = __fadd_rn(e, zp);
       q0 = rhaz(e);
     }
-    if (fabsf(__fsub_rn(hi_of(d), 0.5f)) > 0.5f - 0x1p-14f || !(hi_of(tt) < 4194304.f)) {
+    if (fabsf(hi_of(dh)) > 0.5f - 0x1p-14f) {
       float e = __fdiv_rn(hi_of(v[j]), sk);
       if (has_z) e = __fadd_rn(e, zp);
       q1 = rhaz(e);
