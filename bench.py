@@ -896,12 +896,39 @@ def main() -> None:
     ap.add_argument("--one-step", action="store_true",
                     help="quantize one set once and exit (for an ncu launch list of exactly one step)")
     ap.add_argument("--configs", action="store_true", help="time BASELINE configs 1, 2 and 4 and exit")
+    ap.add_argument("--profile-side", action="store_true",
+                    help="run small cases of the side-path kernels twice and exit (kernel captures)")
     ap.add_argument("--profile-layer", default="",
                     help="M,N: quantize one synthetic GPTQ layer [M,N] twice (one warm-up) and exit -- a small "
                          "case for kernel captures")
     args = ap.parse_args()
     if args.configs:
         run_configs()
+        return
+    if args.profile_side:
+        # small cases of the side-path kernels, for kernel captures: PiSO (4096 x
+        # 4096, INT4 asymmetric), greedy search (1024 x 1024, one pass), SmoothQuant
+        # factors, PermuQuant order and errors (4096 x 16384), SVD split (4096 x 4096, rank 32)
+        import warnings
+        import int_crush_converter_b200 as B
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        g = torch.Generator(device=dev).manual_seed(9)
+        W = torch.randn(4096, 4096, generator=g, device=dev) * 0.02
+        hd = torch.rand(4096, generator=g, device=dev) + 0.1
+        Wg = torch.randn(1024, 1024, generator=g, device=dev) * 0.02
+        Wd = torch.randn(4096, 16384, generator=g, device=dev).half() * 0.02
+        amax = torch.rand(16384, generator=g, device=dev) * 5
+        for _ in range(2):
+            B.compute_piso_scales_int4_asymmetric(W, hd)
+            with warnings.catch_warnings():
+                warnings.simplefilter("ignore")
+                B.ldlq_quantize_layer(Wg, None, block_size=128, int_bits=4, iterations=1, greedy_passes=1)
+            B.compute_smoothing_factors(amax, Wd)
+            B.find_permutation_with_acceptance(Wd, None, 0.5, 128, 0.0, 4)
+            B.decompose_weight(W, rank=32)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_side": "ok"}))
         return
     if args.profile_layer:
         import int_crush_converter_b200 as B

@@ -202,7 +202,7 @@ int ic_group_quant_error(const void* W, int dtype, int64_t M, int64_t N, int64_t
  * svd.decompose_weight calls (torch.svd_lowrank, q = rank, niter = 2); its
  * products run on ic_gemm_tn.  ic_orthonormalize: the columns of X [m, q]
  * (row-major, leading dimension ldx, 1 <= q <= min(m, 64)) made orthonormal in
- * place (modified Gram-Schmidt, twice, fp64 sums) -- the range finder's QR.
+ * place (classical Gram-Schmidt applied twice, fp64 sums) -- the range finder's QR.
  * ic_sym_eig: eigenvalues (descending) and eigenvectors (columns of V) of a
  * symmetric q x q matrix, q <= 64, by cyclic Jacobi -- the SVD of the
  * projected matrix through B B^T. */

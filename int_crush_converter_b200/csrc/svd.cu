@@ -3,7 +3,7 @@
 // an SVD of the small projected matrix).  The products run on the library's
 // 3xTF32 GEMM (host side); the two small dense steps are here:
 //   orth_kernel   -- orthonormal columns of X [m x q] (row-major, q <= 64) by
-//                    modified Gram-Schmidt applied twice, one CTA; the QR
+//                    classical Gram-Schmidt applied twice, one CTA; the QR
 //                    step of the range finder;
 //   jacobi_kernel -- eigenpairs of a symmetric q x q matrix (q <= 64) by cyclic
 //                    Jacobi with all q/2 disjoint rotations of a round applied
@@ -28,25 +28,36 @@ __device__ double block_sum(double v, double* red) {
 }
 
 __global__ void __launch_bounds__(1024) orth_kernel(float* __restrict__ X, int64_t m, int q, int64_t ldx) {
+  // classical Gram-Schmidt applied twice per column ("twice is enough"): the
+  // projections of column j on the earlier columns come from one pass of
+  // per-warp dot products (warp w takes columns w, w + 32, ...), then each
+  // thread subtracts them from its rows in one sweep along the row
   __shared__ double red[32];
-  for (int pass = 0; pass < 2; ++pass) {
-    for (int j = 0; j < q; ++j) {
-      // x_j -= sum_{i<j} (x_i . x_j) x_i, one projection at a time (MGS)
-      for (int i = 0; i < j; ++i) {
+  __shared__ double dots[QMAX];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int j = 0; j < q; ++j) {
+    for (int pass = 0; pass < 2; ++pass) {
+      for (int i = warp; i < j; i += nw) {
         double d = 0.0;
-        for (int64_t r = threadIdx.x; r < m; r += blockDim.x) d += (double)X[r * ldx + i] * (double)X[r * ldx + j];
-        d = block_sum(d, red);
-        for (int64_t r = threadIdx.x; r < m; r += blockDim.x)
-          X[r * ldx + j] = (float)((double)X[r * ldx + j] - d * (double)X[r * ldx + i]);
-        __syncthreads();
+        for (int64_t r = lane; r < m; r += 32) d += (double)X[r * ldx + i] * (double)X[r * ldx + j];
+        d = warp_sum_d(d);
+        if (lane == 0) dots[i] = d;
       }
-      double nn = 0.0;
-      for (int64_t r = threadIdx.x; r < m; r += blockDim.x) nn += (double)X[r * ldx + j] * (double)X[r * ldx + j];
-      nn = block_sum(nn, red);
-      const double inv = nn > 0.0 ? 1.0 / sqrt(nn) : 0.0;
-      for (int64_t r = threadIdx.x; r < m; r += blockDim.x) X[r * ldx + j] = (float)((double)X[r * ldx + j] * inv);
+      __syncthreads();
+      for (int64_t r = threadIdx.x; r < m; r += blockDim.x) {
+        const float* row = X + r * ldx;
+        double x = (double)row[j];
+        for (int i = 0; i < j; ++i) x -= dots[i] * (double)row[i];
+        X[r * ldx + j] = (float)x;
+      }
       __syncthreads();
     }
+    double nn = 0.0;
+    for (int64_t r = threadIdx.x; r < m; r += blockDim.x) nn += (double)X[r * ldx + j] * (double)X[r * ldx + j];
+    nn = block_sum(nn, red);
+    const double inv = nn > 0.0 ? 1.0 / sqrt(nn) : 0.0;
+    for (int64_t r = threadIdx.x; r < m; r += blockDim.x) X[r * ldx + j] = (float)((double)X[r * ldx + j] * inv);
+    __syncthreads();
   }
 }
 

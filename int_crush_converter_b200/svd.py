@@ -5,8 +5,8 @@
 computed with the algorithm the reference calls, torch.svd_lowrank(W, q=r,
 niter=2) (a randomized range finder with two power iterations, then the SVD of
 the projected r x in matrix): every product on the library's 3xTF32 tensor-core
-GEMM, the orthonormalisations by ic_orthonormalize (modified Gram-Schmidt,
-twice), the small SVD through the eigenpairs of B B^T by ic_sym_eig (cyclic
+GEMM, the orthonormalisations by ic_orthonormalize (classical Gram-Schmidt
+applied twice), the small SVD through the eigenpairs of B B^T by ic_sym_eig (cyclic
 Jacobi).  The range finder draws its Gaussian test matrix from torch's CUDA
 generator (the pipeline seeds it, pipeline.py:258-263), so, as with the
 reference on different hardware, the factors are one valid randomized
