@@ -420,6 +420,30 @@ def run_device(args, rank: int, world: int) -> None:
     ms_max = max_over_ranks(e0.elapsed_time(e1), dev)
     value = n_params * args.steps / (ms_max * 1e-3) / 1e6
     launches = int(max_over_ranks(float(launches), dev)) if world > 1 else int(launches)
+    passes3 = None
+    if args.passes3_steps > 0:
+        # the same model pass with the trailing update in 3xTF32 (update_passes=3)
+        def fetch3(i):
+            W, H, kw = fetch(i)
+            return W, H, dict(kw, update_passes=3)
+        pool.fork()
+        run_model_steps(args, "p3w", 1, layers, order, fetch3, pool, world, dev)
+        pool.check()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        pool.fork()
+        run_model_steps(args, "p3t", args.passes3_steps, layers, order, fetch3, pool, world, dev)
+        f1.record()
+        torch.cuda.synchronize(dev)
+        pool.check()
+        ms3 = max_over_ranks(f0.elapsed_time(f1), dev)
+        passes3 = {"value": round(n_params * args.passes3_steps / (ms3 * 1e-3) / 1e6, 3), "unit": "Mparams/s",
+                   "steps": args.passes3_steps, "ms_per_step": round(ms3 / args.passes3_steps, 3),
+                   "note": "GPTQ trailing update in 3xTF32 (update_passes=3) instead of one TF32 pass with fp32 "
+                           "accumulation; everything else as the headline"}
     del sets
     torch.cuda.empty_cache()
 
@@ -457,6 +481,7 @@ def run_device(args, rank: int, world: int) -> None:
                        model_sets=args.model_sets, params=n_params, order=args.order),
         "e2e": e2e,
         "dropin_e2e": dropin,
+        "trailing_update_3xtf32": passes3,
         "other_configs": other,
         "gpu_launches": launches,
         "inverse_graphs_instantiated_in_timed_region": int(graphs),
@@ -880,6 +905,8 @@ def main() -> None:
     ap.add_argument("--model-sets", type=int, default=MODEL_SETS, help="linear sets in the model (config 5: 40)")
     ap.add_argument("--order", default="lpt", choices=["lpt", "natural"], help="work-queue order of the layers")
     ap.add_argument("--depth", type=int, default=6, help="layers a rank keeps unfinished on its GPU")
+    ap.add_argument("--passes3-steps", type=int, default=2,
+                    help="also time this many model passes with the 3xTF32 trailing update")
     ap.add_argument("--dropin", type=int, default=1, help="also time the reference call shape (drop-in API)")
     ap.add_argument("--other-configs", type=int, default=1,
                     help="also measure configs 1, 2 and 4 (rank 0) with the reference's CPU samples")
