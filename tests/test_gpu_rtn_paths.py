@@ -4,7 +4,7 @@ packed fp32 pair instructions), the fast kernel (=1; one scale per row,
 rot 16 / 64 / 256, deferred Hadamard scaling, shared-memory transpose) and the
 register kernel (=0).  Codes, packed bytes, scales, zero-points and verify
 statistics must be bit-identical on every mode (INT4/INT8,
-symmetric/asymmetric, clipping-ratio search, padding, outliers above the
+symmetric/asymmetric, clipping-ratio search incl. small ratios, padding, outliers above the
 sanitize clamp, NaN rows, fp16/bf16/fp32 inputs)."""
 
 import os
@@ -32,6 +32,9 @@ CASES = [
     (48, 3072, 64, 8, False, RATIOS, "bfloat16"),
     (24, 2048, 256, 4, False, RATIOS, "half"),
     (24, 1024, 64, 8, True, None, "float"),
+    # ratios small enough that |v / s| exceeds the range of the uncorrected quotient
+    (32, 3072, 64, 8, False, [0.3, 0.6, 1.0], "half"),
+    (32, 4096, 256, 8, True, [0.5, 1.0], "half"),
 ]
 
 CHILD = r"""
