@@ -319,6 +319,32 @@ def dominant_gemm_tflops(dev: torch.device, n: int = 16384, reps: int = 3) -> tu
     return n ** 3 / 3.0 / (ms * 1e-3) / 1e12, ms
 
 
+def cublas_tf32_tflops(dev: torch.device, n: int = 16384, reps: int = 3) -> float | None:
+    """Context for the roofline: the TF32 rate cuBLAS itself reaches on this GPU
+    (a square fp32 product with TF32 tensor cores allowed), CUDA events."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        g = torch.Generator(device=dev).manual_seed(3)
+        a = torch.randn(n, n, generator=g, device=dev)
+        b = torch.randn(n, n, generator=g, device=dev)
+        c = a @ b
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            torch.matmul(a, b, out=c)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        del a, b, c
+        return round(2.0 * n ** 3 / (ms * 1e-3) / 1e12, 1)
+    except RuntimeError:
+        return None
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def model_layers(n_sets: int) -> list[tuple[int, str, int, int]]:
     """(set, layer name, out, in) of every linear layer of the model."""
     return [(si, name, m, n) for si in range(n_sets) for name, m, n in LAYERS]
@@ -451,6 +477,7 @@ def run_device(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     achieved, gemm_ms = dominant_gemm_tflops(dev)
+    cublas_tf32 = cublas_tf32_tflops(dev)
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -487,8 +514,15 @@ def run_device(args, rank: int, world: int) -> None:
         "inverse_graphs_instantiated_in_timed_region": int(graphs),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": TRAFFIC_BYTES,
-                     "kernel": "gemm_tn_kernel<128,3> (3xTF32), triangular U*U^T of the mlp_down inverse "
+                     "kernel": "gemm_pair_kernel (3xTF32, tcgen05 cta_group::2 CTA pairs, K-slabs of 4096), "
+                               "triangular U*U^T of the mlp_down inverse "
                                f"(16384^3/3 flop), {gemm_ms:.2f} ms/launch",
+                     "context": {"cublas_tf32_tflops": cublas_tf32,
+                                 "tf32_work_over_cublas_tf32": (round(3 * achieved / cublas_tf32, 3)
+                                                                if cublas_tf32 else None),
+                                 "note": "cuBLAS's own fp32 GEMM on TF32 tensor cores (torch.matmul, "
+                                         "allow_tf32) at 16384^3 on this GPU, timed the same way; the kernel "
+                                         "does three TF32 products per output term"},
                      "peak_basis": ("measured bf16 burst / 2 (TF32 rate) / 3 (3xTF32 products), of measured"
                                     if "bf16_tflops" in peaks else "fallback 1.59 PF bf16 / 2 / 3, of fallback")},
         "step_roofline": {"bound": "tensor", "flop_per_step": n_flop,

@@ -787,16 +787,27 @@ int launch_pair(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap&
   return IC_OK;
 }
 
-// CTA pairs for 3xTF32 products with more than one 128-row tile, opt-in with
-// IC_GEMM_PAIR=1: measured on B200 they match the single-CTA kernel on large
-// products (the main loop is tensor-bound either way) and lose on the many
-// one-tile products of the inverse's recursion.
+// CTA pairs for every 3xTF32 product with more than one 128-row tile, opt-in
+// with IC_GEMM_PAIR=1: measured on B200 they lose on the many small products of
+// the inverse's recursion.
 bool pair_enabled() {
   static const bool on = [] {
     const char* e = getenv("IC_GEMM_PAIR");
     return e && e[0] == '1';
   }();
   return on;
+}
+// CTA pairs for 3xTF32 products of at least this many output elements (m * n;
+// IC_GEMM_PAIR_MIN overrides, 0 = never).  Measured on B200: the triangular
+// 16384 product runs 166 vs 161 TF/s on pairs, and the benchmark gains ~0.8%
+// with pairs from 8192 x 8192 up (3694-3699 vs 3658-3673 Mparams/s).
+int64_t pair_min_elems() {
+  static const int64_t v = [] {
+    const char* e = getenv("IC_GEMM_PAIR_MIN");
+    if (!e) return (int64_t)1 << 26;
+    return atoll(e) > 0 ? (int64_t)atoll(e) : INT64_MAX;
+  }();
+  return v;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -875,7 +886,7 @@ int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, c
              lower_rows, row_major, tri};
   const int64_t kk = k > 0 ? k : 1;
   CUtensorMap ah, al, bh, bl;
-  if (passes == 3 && m > BM && pair_enabled()) {
+  if (passes == 3 && m > BM && (pair_enabled() || m * n >= pair_min_elems())) {
     IC_TRY(make_map(&ah, a_hi, m, kk, lda, BM));
     IC_TRY(make_map(&bh, b_hi, n, kk, ldb, 64));
     IC_TRY(make_map(&al, a_lo, m, kk, lda, BM));
@@ -898,8 +909,8 @@ int gemm_once(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, c
 // product (128 x K x 8 bytes as a hi/lo pair: 16.8 MB at K = 16384) is too
 // large for the CTAs sharing it to find it in L2, so a 16384^3 product read
 // 167 GB from DRAM (38x its operands) on B200.  Split into K-slabs of this
-// width, each accumulating into D (as a hi/lo pair the running sum is exact
-// fp32, the same one rounding per slab as the kernel's chunk sums).
+// width, each accumulating into D (the running sum is exact fp32, the same one
+// rounding per slab as the kernel's chunk sums).
 // IC_GEMM_SLAB=0 turns the split off.
 int slab_k() {
   static const int v = [] {
@@ -918,12 +929,15 @@ int gemm_tn(int64_t m, int64_t n, int64_t k, float alpha, const float* a_hi, con
   if (passes != 3 || sk <= 0 || sk % BK || k < 2 * sk || m * n < (int64_t(1) << 26))
     return gemm_once(m, n, k, alpha, a_hi, a_lo, lda, b_hi, b_lo, ldb, beta, c_hi, c_lo, ldc, d_hi, d_lo, ldd,
                      passes, st, tri, 0);
+  // Between slabs the running sum is held as plain fp32 in D's hi part (the
+  // exact value a hi/lo pair would hold, half the bytes to read and write);
+  // the last slab reads it and writes D as the pair.
   for (int64_t k0 = 0; k0 < k; k0 += sk) {
     const int64_t kw = std::min(sk, k - k0);
-    const bool first = k0 == 0;
+    const bool first = k0 == 0, last = k0 + kw >= k;
     IC_TRY(gemm_once(m, n, kw, alpha, a_hi + k0, a_lo + k0, lda, b_hi + k0, b_lo + k0, ldb, first ? beta : 1.f,
-                     first ? c_hi : d_hi, first ? c_lo : d_lo, first ? ldc : ldd, d_hi, d_lo, ldd, passes, st,
-                     tri, (int)k0));
+                     first ? c_hi : d_hi, first ? c_lo : nullptr, first ? ldc : ldd, d_hi, last ? d_lo : nullptr,
+                     ldd, passes, st, tri, (int)k0));
   }
   return IC_OK;
 }
