@@ -715,7 +715,7 @@ def run_hbm_kernels(reps: int = 5) -> None:
     def rot():
         nat.check(lib.ic_rotate_weights(W.data_ptr(), nat.IC_F16, 4096, 16384, 16384, 256, Wr.data_ptr(), 16384, st))
     ms, gbs, frac = timed(rot, 4096 * 16384 * 6)
-    out.append(dict(kernel="rotate_regs_kernel (ic_rotate_weights)", workload="fp16 [4096,16384] -> fp32, rot256",
+    out.append(dict(kernel="rotate_pair256_kernel (ic_rotate_weights)", workload="fp16 [4096,16384] -> fp32, rot256",
                     ms_per_call=ms, achieved_gbs=gbs, frac=frac))
     del W, Wr
     n = 16384
@@ -726,7 +726,7 @@ def run_hbm_kernels(reps: int = 5) -> None:
     def roth():
         nat.check(lib.ic_rotate_hessian(H.data_ptr(), 1, n, n, 256, hh.data_ptr(), hl.data_ptr(), n, st))
     ms, gbs, frac = timed(roth, n * n * 12)
-    out.append(dict(kernel="rotate_regs_kernel + hess_cols256_kernel (ic_rotate_hessian)",
+    out.append(dict(kernel="rotate_pair256_kernel + hess_cols256_kernel (ic_rotate_hessian)",
                     workload="fp32 H [16384,16384] -> hi/lo pair, rot256", ms_per_call=ms, achieved_gbs=gbs,
                     frac=frac))
     for o in out:

@@ -2,6 +2,7 @@
 // (or a 32-column strip of rot rows) being rotated lives in shared memory,
 // so HBM sees each element once per pass.
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "hadamard.cuh"
@@ -105,11 +106,174 @@ __global__ void __launch_bounds__(256) rotate_regs_kernel(const T* __restrict__ 
   }
 }
 
+// rot = 256 with two groups per 16-lane team: lane l holds chunk l (16
+// elements) of two neighbouring groups of a row as fp32 pairs, so every
+// butterfly of both groups is one packed .f32x2 instruction; the two lane
+// digits go through one 16 x 16 shared-memory transpose of pairs instead of
+// shuffles.  Same stage order and fp32 operations as rotate_regs_kernel
+// (digits of the element index inside the chunk, then of the chunk index;
+// the factor 1/16 once at the end): bit-identical output.  Rows are `nb`
+// batches of `rows` rows of which the first `valid` exist in the source;
+// columns >= N are zero padding; npad % 512 == 0.
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 pk2(float a, float b) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float lo2(f2 r) { return __uint_as_float((uint32_t)(r & 0xffffffffull)); }
+__device__ __forceinline__ float hi2(f2 r) { return __uint_as_float((uint32_t)(r >> 32)); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ void h4pair(f2& x0, f2& x1, f2& x2, f2& x3) {
+  const f2 p = add2(x0, x1), m = sub2(x0, x1), P = add2(x2, x3), Mm = sub2(x2, x3);
+  x0 = add2(p, Mm);
+  x1 = sub2(p, Mm);
+  x2 = add2(m, P);
+  x3 = sub2(P, m);
+}
+
+// 16 elements of one chunk as fp32 (zero past N or for padding rows)
+template <typename T>
+__device__ __forceinline__ void load_chunk16(const T* p, bool in_row, int64_t col, int64_t N, float (&x)[16]) {
+  constexpr int V = 16 / sizeof(T);
+  if (in_row && col + 16 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 16 / V; ++q) {
+      const uint4 raw = reinterpret_cast<const uint4*>(p)[q];
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int u = 0; u < V; ++u) x[q * V + u] = load_as_f32(e + u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = (in_row && col + j < N) ? load_as_f32(p + j) : 0.f;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) rotate_pair256_kernel(const T* __restrict__ src, int64_t N, int64_t ld,
+                                                             int64_t bstride, int64_t rows, int64_t valid,
+                                                             int64_t nb, float* __restrict__ out, int64_t ldo,
+                                                             int64_t ostride, int64_t npad, float clamp,
+                                                             const float* __restrict__ smw,
+                                                             const float* __restrict__ smh) {
+  __shared__ __align__(16) f2 tr[16][256];  // one 16 x 16 tile of pairs per 16-lane team
+  const int team = threadIdx.x >> 4, l = threadIdx.x & 15;
+  f2* tile = tr[team];
+  const int64_t pairs_per_row = npad / 512;
+  const int64_t tasks = nb * rows * pairs_per_row;
+  const int64_t teams = (int64_t)gridDim.x * (blockDim.x >> 4);
+  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 4) + team; task - (team & 1) < tasks; task += teams) {
+    // every lane of the warp runs the same number of iterations (the transpose
+    // needs the whole half-warp), tasks past the end compute zeros
+    const bool act = task < tasks;
+    const int64_t rg = act ? task / pairs_per_row : 0;  // batch-row
+    const int64_t j = act ? task - rg * pairs_per_row : 0;
+    const int64_t b = rg / rows, r = rg - b * rows;
+    const int64_t ca = j * 512 + 16 * l, cb = ca + 256;  // chunk l of groups 2j and 2j + 1
+    const bool in_row = act && r < valid;
+    f2 v[16];
+    {
+      float x[16], y[16];
+      const T* rowp = src + b * bstride + r * ld;
+      load_chunk16(rowp + ca, in_row, ca, N, x);
+      load_chunk16(rowp + cb, in_row, cb, N, y);
+      if (clamp > 0.f) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          x[e] = fabsf(x[e]) > clamp ? 0.f : x[e];
+          y[e] = fabsf(y[e]) > clamp ? 0.f : y[e];
+        }
+      }
+      if (smw && act) {  // SmoothQuant: W[:, c] * s_c (smoothquant.py:54-69)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          if (ca + e < N) x[e] = __fmul_rn(x[e], smw[ca + e]);
+          if (cb + e < N) y[e] = __fmul_rn(y[e], smw[cb + e]);
+        }
+      }
+      if (smh && in_row) {  // H / max(s_i s_j, 1e-16), capped at 1e30 (pipeline.py:99-137)
+        const float si = smh[r];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          if (ca + e < N) x[e] = smooth_hessian(x[e], si, smh[ca + e]);
+          if (cb + e < N) y[e] = smooth_hessian(y[e], si, smh[cb + e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = pk2(x[e], y[e]);
+    }
+    // digits of the element index inside the chunk
+#pragma unroll
+    for (int q = 0; q < 4; ++q) h4pair(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) h4pair(v[q], v[4 + q], v[8 + q], v[12 + q]);
+    // transpose: element (l, e) to row e, pair slot 2 * (((l >> 1) + e) & 7) + (l & 1);
+    // lane l then reads row l (element index l inside every chunk) as eight
+    // 16-byte chunks starting at chunk l (distinct banks per quarter-warp)
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) tile[e * 16 + 2 * (((l >> 1) + e) & 7) + (l & 1)] = v[e];
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 w = *reinterpret_cast<const uint4*>(tile + l * 16 + 2 * ((c + l) & 7));
+      v[2 * c] = ((f2)w.y << 32) | w.x;
+      v[2 * c + 1] = ((f2)w.w << 32) | w.z;
+    }
+    // v[c] = element l of chunk c: digits of the chunk index
+#pragma unroll
+    for (int c = 0; c < 4; ++c) h4pair(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) h4pair(v[u], v[4 + u], v[8 + u], v[12 + u]);
+    if (act) {
+      const f2 S = pk2(0.0625f, 0.0625f);
+      float* o = out + b * ostride + r * ldo + j * 512 + l;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const f2 y = mul2(v[c], S);
+        o[16 * c] = lo2(y);
+        o[256 + 16 * c] = hi2(y);
+      }
+    }
+  }
+}
+
+// IC_ROT_PAIR=0 keeps rot = 256 on rotate_regs_kernel (A/B checks)
+bool rot_pair_on() {
+  static const bool on = [] {
+    const char* e = getenv("IC_ROT_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <typename T>
 void launch_rotate_regs(const T* src, int64_t N, int64_t ld, int64_t bstride, int64_t rows, int64_t valid,
                         int64_t nb, int rot, float* out, int64_t ldo, int64_t ostride, int64_t npad,
                         cudaStream_t st, float clamp = 0.f, const float* smw = nullptr,
                         const float* smh = nullptr) {
+  if (rot == 256 && npad % 512 == 0 && rot_pair_on()) {
+    const int64_t tasks = nb * rows * (npad / 512);
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(tasks, 16), 148 * 8);
+    rotate_pair256_kernel<T><<<grid, 256, 0, st>>>(src, N, ld, bstride, rows, valid, nb, out, ldo, ostride, npad,
+                                                   clamp, smw, smh);
+    return;
+  }
   const int64_t tasks = cdiv(nb * rows * (npad / rot), (int64_t)(32 / (rot / 16)));
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(tasks, 8), 148 * 16);
   rotate_regs_kernel<T><<<grid, 256, 0, st>>>(src, N, ld, bstride, rows, valid, nb, rot, out, ldo, ostride, npad,
