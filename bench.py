@@ -900,12 +900,13 @@ def reference_cpu_configs() -> list[dict]:
     return out
 
 
-def run_configs() -> None:
-    """Configs 1, 2 and 4 (one JSON line each), with the reference's CPU samples."""
+def run_configs(with_reference: bool = True) -> None:
+    """Configs 1, 2 and 4 (one JSON line each), with the reference's CPU samples
+    unless ``with_reference`` is off (device-only runs, e.g. under a profiler)."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peak = _peaks().get("hbm_gbs")
-    cpu = {c["config"]: c for c in reference_configs_subprocess()}
+    cpu = {c["config"]: c for c in reference_configs_subprocess()} if with_reference else {}
     for d in measure_configs(dev, peak):
         d["cpu_baseline"] = cpu.get(d["config"])
         print(json.dumps(d), flush=True)
@@ -957,6 +958,8 @@ def main() -> None:
     ap.add_argument("--one-step", action="store_true",
                     help="quantize one set once and exit (for an ncu launch list of exactly one step)")
     ap.add_argument("--configs", action="store_true", help="time BASELINE configs 1, 2 and 4 and exit")
+    ap.add_argument("--no-ref", action="store_true",
+                    help="with --configs: skip the reference's CPU samples (device work only)")
     ap.add_argument("--profile-side", action="store_true",
                     help="run small cases of the side-path kernels twice and exit (kernel captures)")
     ap.add_argument("--profile-layer", default="",
@@ -964,7 +967,7 @@ def main() -> None:
                          "case for kernel captures")
     args = ap.parse_args()
     if args.configs:
-        run_configs()
+        run_configs(with_reference=not args.no_ref)
         return
     if args.profile_side:
         # small cases of the side-path kernels, for kernel captures: PiSO (4096 x

@@ -8,6 +8,8 @@
 // already updated in this pass (no periodic recompute, no drift).  Candidates
 // g in [qmin, qmax] are evaluated in ascending order with the reference's
 // cost (e+(g-q)s)^2 H_jj + 2 (e+(g-q)s) cross; the first minimum wins.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -26,6 +28,7 @@ struct GArgs {
   float* e_lo;
   int64_t lde;
   const float* cross;
+  const float* cross2;  // second K half of the cross terms (split product), or null
   int64_t ldx;
   const float* h_hi;
   const float* h_lo;
@@ -55,7 +58,9 @@ __global__ void __launch_bounds__(128) greedy_block_kernel(const GArgs a) {
   for (int c = 0; c < GROUP; ++c) {
     const bool ok = cbase + c < bc;
     const int64_t col = a.j0 + cbase + c;
-    cr[c] = ok ? a.cross[rr * a.ldx + cbase + c] : 0.f;
+    cr[c] = ok ? (a.cross2 ? __fadd_rn(a.cross[rr * a.ldx + cbase + c], a.cross2[rr * a.ldx + cbase + c])
+                           : a.cross[rr * a.ldx + cbase + c])
+               : 0.f;
     er[c] = ok ? __fadd_rn(a.e_hi[rr * a.lde + col], a.e_lo[rr * a.lde + col]) : 0.f;
     q[c] = ok ? (float)a.Q[rr * a.ldq + col] : 0.f;
     s[c] = ok ? a.S[rr * a.lds + col] : 0.f;
@@ -127,6 +132,38 @@ __global__ void err_init_kernel(const float* __restrict__ W, int64_t ldw, const 
 
 constexpr size_t GSMEM = (size_t)GB * GB * 4 + (size_t)GB * GROUP * 4;
 
+// The cross-term product of a block (M x 128 outputs, K = N) has one 128-row
+// tile per 128 rows: at M = 8192 that is 64 CTAs on 148 SMs.  Its K range is
+// split in two halves issued on the caller's stream and a side stream (event
+// fork / join), so both halves run at once on twice the SMs; the block kernel
+// adds the two partial sums (first half first).  IC_GREEDY_SPLIT=0 keeps one
+// product.
+bool split_on() {
+  static const bool on = [] {
+    const char* e = getenv("IC_GREEDY_SPLIT");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+struct SideStream {
+  cudaStream_t st = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+// one side stream and event pair per host thread and device
+int side_stream(SideStream** out) {
+  thread_local SideStream cache[64];
+  int dev = 0;
+  IC_CUDA(cudaGetDevice(&dev));
+  SideStream& s = cache[dev & 63];
+  if (!s.st) {
+    IC_CUDA(cudaStreamCreateWithFlags(&s.st, cudaStreamNonBlocking));
+    IC_CUDA(cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming));
+    IC_CUDA(cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming));
+  }
+  *out = &s;
+  return IC_OK;
+}
+
 }  // namespace
 }  // namespace ic
 
@@ -134,7 +171,7 @@ using namespace ic;
 
 extern "C" size_t ic_greedy_workspace_size(int64_t M, int64_t N) {
   const int64_t lde = (N + 3) & ~int64_t(3);
-  return (size_t)M * lde * 4 * 2 + (size_t)M * GB * 4 + 4096;
+  return (size_t)M * lde * 4 * 2 + (size_t)M * GB * 4 * 2 + 4096;
 }
 
 extern "C" int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq, const float* scale2d, int64_t lds,
@@ -151,6 +188,11 @@ extern "C" int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq
   float* eh = cv.take<float>((size_t)M * lde);
   float* el = cv.take<float>((size_t)M * lde);
   float* cross = cv.take<float>((size_t)M * GB);
+  float* cross2 = cv.take<float>((size_t)M * GB);
+  const int64_t kh = (N / 2) & ~int64_t(31);
+  const bool split = split_on() && kh >= 1024 && 2 * cdiv(M, 128) <= 160;
+  SideStream* side = nullptr;
+  if (split) IC_TRY(side_stream(&side));
   static std::atomic<unsigned long long> attr{0};
   IC_TRY(once_per_device(attr, [&]() -> int {
       IC_CUDA(cudaFuncSetAttribute(greedy_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GSMEM));
@@ -164,9 +206,21 @@ extern "C" int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq
   for (int p = 0; p < passes; ++p) {
     for (int64_t j0 = 0; j0 < N; j0 += GB) {
       const int bc = (int)std::min<int64_t>(GB, N - j0);
-      IC_TRY(gemm_tn(M, bc, N, 1.f, eh, el, lde, h_hi + j0 * ldh, h_lo + j0 * ldh, ldh, 0.f, nullptr, nullptr, GB,
-                     cross, nullptr, GB, gemm_passes, st));
-      GArgs a{Q, ldq, scale2d, lds, eh, el, lde, cross, GB, h_hi, h_lo, ldh, M, j0, bc, (float)qmin, (float)qmax};
+      if (split) {
+        IC_CUDA(cudaEventRecord(side->fork, st));
+        IC_CUDA(cudaStreamWaitEvent(side->st, side->fork, 0));
+        IC_TRY(gemm_tn(M, bc, kh, 1.f, eh, el, lde, h_hi + j0 * ldh, h_lo + j0 * ldh, ldh, 0.f, nullptr, nullptr, GB,
+                       cross, nullptr, GB, gemm_passes, st));
+        IC_TRY(gemm_tn(M, bc, N - kh, 1.f, eh + kh, el + kh, lde, h_hi + j0 * ldh + kh, h_lo + j0 * ldh + kh, ldh,
+                       0.f, nullptr, nullptr, GB, cross2, nullptr, GB, gemm_passes, side->st));
+        IC_CUDA(cudaEventRecord(side->join, side->st));
+        IC_CUDA(cudaStreamWaitEvent(st, side->join, 0));
+      } else {
+        IC_TRY(gemm_tn(M, bc, N, 1.f, eh, el, lde, h_hi + j0 * ldh, h_lo + j0 * ldh, ldh, 0.f, nullptr, nullptr, GB,
+                       cross, nullptr, GB, gemm_passes, st));
+      }
+      GArgs a{Q, ldq, scale2d, lds, eh, el, lde, cross, split ? cross2 : nullptr, GB, h_hi, h_lo, ldh, M, j0, bc,
+              (float)qmin, (float)qmax};
       greedy_block_kernel<<<(unsigned)cdiv(M, GROUP), 128, GSMEM, st>>>(a);
       IC_CHECK_LAUNCH();
     }
