@@ -316,6 +316,18 @@ int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq, const flo
                   int64_t N, int passes, int qmin, int qmax, int gemm_passes, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* One pass of the low-rank greedy search (converter/greedy.py:100-199, launched
+ * per 64 columns by greedy_lowrank_triton, greedy.py:384-479): H ~ U_k
+ * diag(s_k) U_k^T plus the exact diagonal.  Per row, for every column in
+ * order: cross = err_lr . (s_k * U_k[j]) - err_j H_jj, candidates in
+ * [qmin,qmax] ascending with cost ne^2 H_jj + 2 ne cross (strict < against
+ * 1e30), then err_j and err_lr += delta U_k[j].  err fp32 [M,N] (Q*s - W),
+ * Q int8, err_lr fp32 [M,k] = err U_k, all updated in place; hdiag [N]; U and
+ * SU = s_k * U fp32 [N,k] row-major; 1 <= k <= 64. */
+int ic_greedy_lowrank_pass(float* err, int64_t lde, int8_t* Q, int64_t ldq, const float* scale2d,
+                           int64_t lds, const float* hdiag, const float* U, const float* SU, int k,
+                           float* err_lr, int64_t M, int64_t N, int qmin, int qmax, void* stream);
+
 /* -------------------------------------------------------------------- PiSO */
 /* PiSO per-row scale search (converter/piso.py:29-182): coarse candidates
  * base*coarse[i], then fine candidates best*fine[i]; cost sum_d h_d (w_d -

@@ -79,6 +79,8 @@ SIGNATURES = {
                            _vp, _i64, _i32, _vp, _sz, _vp]),
     "ic_ldlq_update_scales": (_i32, [_vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _vp]),
     "ic_greedy_workspace_size": (_sz, [_i64, _i64]),
+    "ic_greedy_lowrank_pass": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i64,
+                                      _i32, _i32, _vp]),
     "ic_greedy_run": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32,
                              _i32, _i32, _vp, _sz, _vp]),
     "ic_piso": (_i32, [_vp, _i64, _i64, _i64, _vp, _i32, _i32, _i32, _f32, _vp, _i32, _vp, _i32, _vp,

@@ -35,3 +35,12 @@ W_NONZERO_THRESHOLD = 1e-8       # ldlq.py:505
 GEMM_PASSES = 3
 # Columns per super-block of the two-level lazy update (multiple of the block size).
 SUPERBLOCK = 1024
+
+# Low-rank greedy (greedy.py:293-381, config.py:124-137)
+EIGENVALUE_FLOOR = 1e-12
+STALL_THRESHOLD = 0.99
+LOWRANK_MAX_RANK_FRAC = 0.3
+LOWRANK_MAX_K = 512
+# Sketch width of the low-rank decomposition here: the small eigenproblem runs in
+# one CTA's shared memory (ic_sym_eig), which bounds it at 64 columns.
+LOWRANK_SKETCH = 64

@@ -132,6 +132,95 @@ __global__ void err_init_kernel(const float* __restrict__ W, int64_t ldw, const 
 
 constexpr size_t GSMEM = (size_t)GB * GB * 4 + (size_t)GB * GROUP * 4;
 
+// ---------------------------------------------------------------------------
+// Low-rank pass (converter/greedy.py:100-199, the kernel greedy_lowrank_triton
+// launches per 64 columns, greedy.py:440-462): H ~ U_k diag(s_k) U_k^T + the
+// exact diagonal.  Each thread owns one row: its projection err_lr = err U_k
+// (k <= KMAX values) stays in registers for the whole pass; for every column
+// j in order
+//   cross = sum_i err_lr_i (s_i U[j,i]) - err_j H_jj
+//   g in [qmin, qmax] ascending, cost = ne^2 H_jj + 2 ne cross with
+//   ne = err_j + (g - q_j) max(s_rj, 1e-8); strict < against 1e30, so the
+//   first minimum wins and q_j stays when no cost is below 1e30
+//   err_j += (g - q_j) s;  err_lr_i += delta U[j,i]
+// The rows s_i U[j,i] and U[j,i] of a 64-column block are staged in shared
+// memory and read by every thread (broadcast).
+constexpr int LR_COLS = 64;
+
+struct LArgs {
+  float* err;  // [M, N] Q * s - W, updated
+  int64_t lde;
+  int8_t* Q;
+  int64_t ldq;
+  const float* S;
+  int64_t lds;
+  const float* hdiag;  // [N]
+  const float* U;      // [N, k] eigenvectors
+  const float* SU;     // [N, k] s_i * U[j, i]
+  int k;
+  float* elr;  // [M, k] err U_k, updated
+  int64_t M, N;
+  float qmin, qmax;
+};
+
+template <int KMAX>
+__global__ void __launch_bounds__(128) greedy_lowrank_kernel(const LArgs a) {
+  __shared__ float su_s[LR_COLS][KMAX];
+  __shared__ float u_s[LR_COLS][KMAX];
+  __shared__ float h_s[LR_COLS];
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool rv = r < a.M;
+  const int k = a.k;
+  float e_lr[KMAX];
+#pragma unroll
+  for (int i = 0; i < KMAX; ++i) e_lr[i] = (rv && i < k) ? a.elr[r * k + i] : 0.f;
+  for (int64_t j0 = 0; j0 < a.N; j0 += LR_COLS) {
+    const int nc = (int)((a.N - j0) < LR_COLS ? (a.N - j0) : LR_COLS);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nc * KMAX; idx += blockDim.x) {
+      const int c = idx / KMAX, i = idx - c * KMAX;
+      su_s[c][i] = i < k ? a.SU[(j0 + c) * k + i] : 0.f;
+      u_s[c][i] = i < k ? a.U[(j0 + c) * k + i] : 0.f;
+    }
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) h_s[c] = a.hdiag[j0 + c];
+    __syncthreads();
+    if (!rv) continue;
+    for (int c = 0; c < nc; ++c) {
+      const int64_t j = j0 + c;
+      float cross = 0.f;
+#pragma unroll
+      for (int i = 0; i < KMAX; ++i)
+        if (i < k) cross = __fmaf_rn(e_lr[i], su_s[c][i], cross);
+      const float ej = a.err[r * a.lde + j];
+      const float hjj = h_s[c];
+      cross = __fsub_rn(cross, __fmul_rn(ej, hjj));
+      const float sj = fmaxf(a.S[r * a.lds + j], 1e-8f);
+      const float qo = (float)a.Q[r * a.ldq + j];
+      float best = 1e30f, bq = qo;
+      for (float g = a.qmin; g <= a.qmax; g += 1.f) {
+        const float ne = __fadd_rn(ej, __fmul_rn(__fsub_rn(g, qo), sj));
+        const float cost = __fadd_rn(__fmul_rn(__fmul_rn(ne, ne), hjj), __fmul_rn(__fmul_rn(2.f, ne), cross));
+        if (cost < best) {
+          best = cost;
+          bq = g;
+        }
+      }
+      bq = fminf(fmaxf(bq, a.qmin), a.qmax);
+      const float d = __fmul_rn(__fsub_rn(bq, qo), sj);
+      a.Q[r * a.ldq + j] = (int8_t)bq;
+      a.err[r * a.lde + j] = __fadd_rn(ej, d);
+#pragma unroll
+      for (int i = 0; i < KMAX; ++i)
+        if (i < k) e_lr[i] = __fmaf_rn(d, u_s[c][i], e_lr[i]);
+    }
+  }
+  if (rv) {
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i)
+      if (i < k) a.elr[r * k + i] = e_lr[i];
+  }
+}
+
 // The cross-term product of a block (M x 128 outputs, K = N) has one 128-row
 // tile per 128 rows: at M = 8192 that is 64 CTAs on 148 SMs.  Its K range is
 // split in two halves issued on the caller's stream and a side stream (event
@@ -225,5 +314,23 @@ extern "C" int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq
       IC_CHECK_LAUNCH();
     }
   }
+  return IC_OK;
+}
+
+extern "C" int ic_greedy_lowrank_pass(float* err, int64_t lde, int8_t* Q, int64_t ldq, const float* scale2d,
+                                      int64_t lds, const float* hdiag, const float* U, const float* SU, int k,
+                                      float* err_lr, int64_t M, int64_t N, int qmin, int qmax, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M <= 0 || N <= 0) return IC_OK;
+  if (k < 1 || k > 64) return fail(IC_ERR_UNSUPPORTED, "greedy low-rank: rank must be in [1, 64], got %d", k);
+  if (M > INT32_MAX) return fail(IC_ERR_UNSUPPORTED, "greedy: too many rows");
+  if (!err || !Q || !scale2d || !hdiag || !U || !SU || !err_lr) return fail(IC_ERR_INVALID, "greedy: null operand");
+  LArgs a{err, lde, Q, ldq, scale2d, lds, hdiag, U, SU, k, err_lr, M, N, (float)qmin, (float)qmax};
+  const unsigned grid = (unsigned)cdiv(M, 128);
+  if (k <= 8) greedy_lowrank_kernel<8><<<grid, 128, 0, st>>>(a);
+  else if (k <= 16) greedy_lowrank_kernel<16><<<grid, 128, 0, st>>>(a);
+  else if (k <= 32) greedy_lowrank_kernel<32><<<grid, 128, 0, st>>>(a);
+  else greedy_lowrank_kernel<64><<<grid, 128, 0, st>>>(a);
+  IC_CHECK_LAUNCH();
   return IC_OK;
 }

@@ -12,6 +12,7 @@ the greedy search run in libintcrush_b200.
 from __future__ import annotations
 
 import math
+import os
 import warnings
 
 import torch
@@ -25,6 +26,7 @@ from .config import (
     W_NONZERO_THRESHOLD,
 )
 from .greedy import greedy_local_search
+from .greedy import greedy_lowrank as greedy_lowrank_search
 from .hessian import dlr_to_dense, hessian_pair, inverse_pair, woodbury_inverse
 from .types import QuantizationResult
 
@@ -116,11 +118,14 @@ def _ls_scales(Q, Wd):  # ldlq.py:227-231, 262-265
 
 def ldlq_quantize_layer(W: torch.Tensor, hessian=None, block_size: int = 128, damping: float = 0.01,
                         int_bits: int = 4, iterations: int = 1, greedy_passes: int = 0,
-                        rank_threshold: float = 0.01) -> QuantizationResult:
+                        rank_threshold: float = 0.01, greedy_lowrank: bool | None = None) -> QuantizationResult:
     """Quantize one weight matrix with LDLQ (ldlq.py:95-279).
 
-    ``rank_threshold`` is accepted for signature compatibility; the greedy
-    search here always uses the full-rank Hessian (as the reference's CPU path).
+    The greedy search uses the full-rank Hessian (the reference's CPU path,
+    the parity oracle) unless ``greedy_lowrank`` (default: the environment
+    variable IC_GREEDY_LOWRANK=1) selects the reference's GPU low-rank variant
+    with ``rank_threshold`` (greedy.py:384-479, dispatched by
+    ldlq._greedy_local_search, ldlq.py:602-647).
     """
     if int_bits not in (4, 8):
         raise ValueError(f"int_bits must be 4 or 8, got {int_bits}")
@@ -191,7 +196,13 @@ def ldlq_quantize_layer(W: torch.Tensor, hessian=None, block_size: int = 128, da
         Q = _single_pass(Wd, hi, lo, ld, flat, block_size, qmin, qmax)
     if greedy_passes > 0:
         gs = _ls_scales(Q, Wd)
-        Q = greedy_local_search(Wd, Q, gs.expand(M, N).contiguous(), H, greedy_passes, qmin, qmax)
+        if greedy_lowrank is None:
+            greedy_lowrank = os.environ.get("IC_GREEDY_LOWRANK", "") == "1"
+        if greedy_lowrank:
+            Q, _, _ = greedy_lowrank_search(Wd, Q, gs.expand(M, N).contiguous(), H, greedy_passes, qmin, qmax,
+                                            rank_threshold=rank_threshold)
+        else:
+            Q = greedy_local_search(Wd, Q, gs.expand(M, N).contiguous(), H, greedy_passes, qmin, qmax)
     fs = _ls_scales(Q, Wd)
     d = Wd - Q.float() * fs
     return QuantizationResult(quantized_W=back(Q, W), scales=back(fs.to(SCALE_DTYPE), W), zero_points=None,

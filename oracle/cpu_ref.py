@@ -722,6 +722,68 @@ def greedy_local_search(W, Q, scale_2d, H, num_passes, clamp_min, clamp_max):  #
     return np.clip(Q, clamp_min, clamp_max).astype(np.int8)
 
 
+def _fma32(a, b, c):
+    """fp32 a*b + c with one rounding (the product is exact in fp64; the fp64
+    sum is then rounded to fp32, a double rounding that differs from a true
+    fused multiply-add only in rare halfway cases)."""
+    return (a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)).astype(f32)
+
+
+def greedy_lowrank_given(W, Q, scale_2d, H, s_k, U_k, num_passes, clamp_min, clamp_max,
+                         stall=0.99):
+    """The low-rank greedy search of greedy_lowrank_triton (greedy.py:384-479)
+    given its decomposition (s_k, U_k): the per-column step of
+    _greedy_lowrank_kernel (greedy.py:100-199, evaluated here row-vectorised
+    with products and the accumulations err_lr . (s U_j) and err_lr += d U_j
+    as fused multiply-adds, the candidate cost term by term), the proxy
+    (err @ H * err).sum() after every pass and the stop when it improves by
+    less than 1% (greedy.py:464-476).  Returns (int8 codes, passes run)."""
+    W = np.asarray(W, dtype=f32)
+    M, N = W.shape
+    Q = np.asarray(Q, dtype=f32).copy()
+    S = np.asarray(scale_2d, dtype=f32)
+    H = np.asarray(H, dtype=f32)
+    U = np.asarray(U_k, dtype=f32)
+    SU = (U * np.asarray(s_k, dtype=f32)[None, :]).astype(f32)
+    k = U.shape[1]
+    Hd = np.diagonal(H).astype(f32)
+    grid = np.arange(clamp_min, clamp_max + 1, dtype=f32)
+    err = (Q * S - W).astype(f32)
+    elr = (err.astype(np.float64) @ U.astype(np.float64)).astype(f32)
+    prev = np.inf
+    runs = 0
+    for p in range(num_passes):
+        runs += 1
+        for j in range(N):
+            cross = np.zeros(M, dtype=f32)
+            for i in range(k):
+                cross = _fma32(elr[:, i], np.full(M, SU[j, i], dtype=f32), cross)
+            ej = err[:, j].copy()
+            cross = (cross - (ej * Hd[j]).astype(f32)).astype(f32)
+            sj = np.maximum(S[:, j], f32(1e-8))
+            qo = Q[:, j].copy()
+            best = np.full(M, f32(1e30), dtype=f32)
+            bq = qo.copy()
+            for g in grid:
+                ne = (ej + ((g - qo).astype(f32) * sj).astype(f32)).astype(f32)
+                cost = (((ne * ne).astype(f32) * Hd[j]).astype(f32)
+                        + ((f32(2) * ne).astype(f32) * cross).astype(f32)).astype(f32)
+                better = cost < best
+                best = np.where(better, cost, best)
+                bq = np.where(better, g, bq)
+            bq = np.clip(bq, clamp_min, clamp_max).astype(f32)
+            d = ((bq - qo).astype(f32) * sj).astype(f32)
+            Q[:, j] = bq
+            err[:, j] = (ej + d).astype(f32)
+            for i in range(k):
+                elr[:, i] = _fma32(d, np.full(M, U[j, i], dtype=f32), elr[:, i])
+        proxy = float(((err.astype(np.float64) @ H.astype(np.float64)) * err).sum())
+        if p > 0 and proxy >= prev * stall:
+            break
+        prev = proxy
+    return np.clip(Q, clamp_min, clamp_max).astype(np.int8), runs
+
+
 def _ls_scales(Q, W):  # ldlq.py:227-231, 262-265
     Qf = Q.astype(f32)
     num = (Qf * W).sum(axis=1, keepdims=True, dtype=f32)

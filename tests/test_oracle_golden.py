@@ -200,3 +200,24 @@ def test_permuquant(golden, name):
     assert abs(e0 / float(golden[name + "/err"]) - 1) < 1e-5
     assert abs(e1 / float(golden[name + "/err_perm"]) - 1) < 1e-5
     assert acc == bool(golden[name + "/accepted"])
+
+
+def test_lowrank_greedy_oracle_with_full_decomposition_is_the_full_rank_search():
+    """The low-rank greedy restatement (greedy.py:100-199, 384-479) given every
+    eigenpair of H computes the full-rank coordinate descent of the golden-pinned
+    oracle (greedy.py:487-541): same codes."""
+    rng = np.random.default_rng(0)
+    M, N = 48, 96
+    W = (rng.standard_normal((M, N)) * 0.02).astype(np.float32)
+    W[:, 5] *= 30
+    H = (W.T @ W / M).astype(np.float32)
+    H += np.eye(N, dtype=np.float32) * np.float32(0.01 * np.diag(H).mean())
+    ev, V = np.linalg.eigh(H.astype(np.float64))
+    ev, V = ev[::-1].astype(np.float32), V[:, ::-1].astype(np.float32)
+    s = (np.abs(W).max(1, keepdims=True) / 7).astype(np.float32)
+    Q = np.clip(np.rint(W / s), -8, 7).astype(np.int8)
+    S = np.ascontiguousarray(np.broadcast_to(s, (M, N)))
+    q_lr, runs = R.greedy_lowrank_given(W, Q, S, H, ev, V, 2, -8, 7)
+    q_full = R.greedy_local_search(W, Q, S, H, 2, -8, 7)
+    assert runs == 2
+    assert np.array_equal(q_lr, q_full)
