@@ -47,10 +47,28 @@ __global__ void __launch_bounds__(128) greedy_block_kernel(const GArgs a) {
   const int64_t r = (int64_t)blockIdx.x * GROUP + lane;
   const bool rv = r < a.M;
   const int64_t rr = rv ? r : a.M - 1;
-  for (int idx = threadIdx.x; idx < bc * bc; idx += blockDim.x) {
-    const int j = idx / bc, k = idx % bc;
-    const int64_t o = (a.j0 + j) * a.ldh + a.j0 + k;
-    hs[j * GB + k] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
+  // the block's H[j0 + j, j0 + k] (hi + lo) into shared memory; every
+  // iteration's loads are independent, so they are unrolled to overlap their
+  // latency (16-byte loads when the block is full and aligned)
+  const bool v4 = bc == GB && ((a.ldh | a.j0) & 3) == 0 && (reinterpret_cast<uintptr_t>(a.h_hi) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(a.h_lo) & 15) == 0;
+  if (v4) {
+#pragma unroll 8
+    for (int idx = threadIdx.x; idx < GB * GB / 4; idx += 128) {
+      const int j = idx >> 5, k = (idx & 31) * 4;
+      const int64_t o = (a.j0 + j) * a.ldh + a.j0 + k;
+      const float4 h = *reinterpret_cast<const float4*>(a.h_hi + o);
+      const float4 l = *reinterpret_cast<const float4*>(a.h_lo + o);
+      *reinterpret_cast<float4*>(hs + j * GB + k) =
+          make_float4(__fadd_rn(h.x, l.x), __fadd_rn(h.y, l.y), __fadd_rn(h.z, l.z), __fadd_rn(h.w, l.w));
+    }
+  } else {
+#pragma unroll 8
+    for (int idx = threadIdx.x; idx < bc * bc; idx += blockDim.x) {
+      const int j = idx / bc, k = idx % bc;
+      const int64_t o = (a.j0 + j) * a.ldh + a.j0 + k;
+      hs[j * GB + k] = __fadd_rn(a.h_hi[o], a.h_lo[o]);
+    }
   }
   const int cbase = g * GROUP;
   float cr[GROUP], er[GROUP], q[GROUP], s[GROUP];
