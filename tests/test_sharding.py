@@ -1,5 +1,6 @@
 """Multi-GPU host logic on CPU: layer sharding over ranks (no data-path
-collective) and the max-over-ranks timing reduction, run as two gloo ranks."""
+collective), the work queue and gather, and the max-over-ranks timing reduction,
+run as gloo ranks."""
 
 import os
 import socket
@@ -220,8 +221,8 @@ def _queue_worker(rank, world, port, q):
         torch.distributed.destroy_process_group()
 
 
-def test_two_gloo_ranks_work_queue_and_gather():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_work_queue_and_gather(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -235,13 +236,13 @@ def test_two_gloo_ranks_work_queue_and_gather():
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    taken0, taken1 = res[0][1], res[1][1]
-    assert not set(taken0) & set(taken1)
-    assert sorted(taken0 + taken1) == list(range(7))
-    assert res[0][2] and res[1][2]
+    taken = [r[1] for r in res]
+    flat = [i for t in taken for i in t]
+    assert len(flat) == len(set(flat)) and sorted(flat) == list(range(7))  # every layer exactly once
+    assert all(r[2] for r in res)
     # each rank takes in longest-first order
     costs = [5, 1, 9, 3, 7, 2, 8]
-    for t in (taken0, taken1):
+    for t in taken:
         assert [costs[i] for i in t] == sorted((costs[i] for i in t), reverse=True)
 
 
