@@ -970,24 +970,31 @@ __global__ void __launch_bounds__(128) rtn_pair_kernel(const RtnArgs a) {
           cs = clamp_scale(__fdiv_rn(__fmul_rn(amax, ratio), div));
         }
         const float csk = __fmul_rn(cs, UP), rcs = __frcp_rn(csk);
-        const f2 S = pk(csk, csk), NS = pk(-csk, -csk), RS = pk(rcs, rcs), Z = pk(czp, czp);
+        const f2 S = pk(csk, csk), RS = pk(rcs, rcs), Z = pk(czp, czp);
         const f2 M2 = pk(MAGIC, MAGIC);
+        const float THR = has_z ? 0x1p-13f : 0x1p-14f;
         f2 part2 = 0ull;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const f2 y = quot2(v[j], S, NS, RS, Z, has_z);
+          // y = v * RN(1/s) (+ z), uncorrected: within 3 * 2^-24 * |v/s| of the
+          // IEEE quotient, and a code can only change while |v/s| <= 2^8 + 1
+          // (beyond, both roundings clamp alike), so y is within 4.6e-5 of the
+          // reference's RN(v/s) (+ z) there; a fractional part within THR of
+          // .5 takes the exact division
+          f2 y = mul2(v[j], RS);
+          if (has_z) y = add2(y, Z);
           // round-half-even by the magic add (|y| stays far below 2^22 here:
           // |v| <= the row's absmax and cs >= absmax * 0.8 / 127 up to the
           // scale clamp; a NaN fails the test below and takes the exact path)
           f2 rq = sub2(add2(y, M2), M2);
           const f2 dy = sub2(y, rq);
           float r0 = lo_of(rq), r1 = hi_of(rq);
-          if (!(fabsf(lo_of(dy)) <= 0.5f - 0x1p-14f)) {
+          if (!(fabsf(lo_of(dy)) <= 0.5f - THR)) {
             float e = __fdiv_rn(lo_of(v[j]), csk);
             if (has_z) e = __fadd_rn(e, czp);
             r0 = rintf(e);
           }
-          if (!(fabsf(hi_of(dy)) <= 0.5f - 0x1p-14f)) {
+          if (!(fabsf(hi_of(dy)) <= 0.5f - THR)) {
             float e = __fdiv_rn(hi_of(v[j]), csk);
             if (has_z) e = __fadd_rn(e, czp);
             r1 = rintf(e);
