@@ -800,14 +800,6 @@ __device__ __forceinline__ void h4p(f2& x0, f2& x1, f2& x2, f2& x3) {
   x3 = sub2(P, m);
 }
 __device__ __forceinline__ float clamp_nan(float x, float lo, float hi) { return min_nan(max_nan(x, lo), hi); }
-// y (pair) = corrected quotient v / s (+ z); per lane the IEEE division where
-// the rounding boundary is within 2^-14 (see fast_rhaz / fast_rint_div)
-__device__ __forceinline__ f2 quot2(f2 v, f2 s, f2 ns, f2 rs, f2 z, bool has_z) {
-  const f2 q0 = mul2(v, rs);
-  f2 y = fma2(fma2(q0, ns, v), rs, q0);
-  if (has_z) y = add2(y, z);
-  return y;
-}
 constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
 
 template <typename T, int ROT>
@@ -1039,14 +1031,17 @@ __global__ void __launch_bounds__(128) rtn_pair_kernel(const RtnArgs a) {
   // ---- codes, statistics, packing ----
   const float sk = __fmul_rn(__half2float(__ushort_as_half(s16)), UP);
   const float rsk = __frcp_rn(sk);
-  const f2 S = pk(sk, sk), NS = pk(-sk, -sk), RS = pk(rsk, rsk), Z = pk(zp, zp);
+  const f2 S = pk(sk, sk), RS = pk(rsk, rsk), Z = pk(zp, zp);
   const f2 HALF = pk(0.5f, 0.5f), M2 = pk(MAGIC, MAGIC);
+  const float THR = has_z ? 0x1p-13f : 0x1p-14f;  // as in the clip search
   f2 part2 = 0ull;
   float mx = 0.f;
   uint32_t ca4[4] = {0u, 0u, 0u, 0u}, cb4[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const f2 y = quot2(v[j], S, NS, RS, Z, has_z);
+    // uncorrected quotient, as in the clip search
+    f2 y = mul2(v[j], RS);
+    if (has_z) y = add2(y, Z);
     const f2 ay = pk(fabsf(lo_of(y)), fabsf(hi_of(y)));
     const f2 tt = add2(ay, HALF);
     const f2 fl = sub2(add2_rm(tt, M2), M2);  // floor(|y| + 1/2)
@@ -1056,12 +1051,12 @@ __global__ void __launch_bounds__(128) rtn_pair_kernel(const RtnArgs a) {
     // |y| is bounded by the scale (|v| <= absmax, s >= absmax / 7.x, or the
     // asymmetric range); a NaN passes the test and stays NaN as rhaz(NaN).
     const f2 dh = sub2(d, HALF);
-    if (fabsf(lo_of(dh)) > 0.5f - 0x1p-14f) {
+    if (fabsf(lo_of(dh)) > 0.5f - THR) {
       float e = __fdiv_rn(lo_of(v[j]), sk);
       if (has_z) e = __fadd_rn(e, zp);
       q0 = rhaz(e);
     }
-    if (fabsf(hi_of(dh)) > 0.5f - 0x1p-14f) {
+    if (fabsf(hi_of(dh)) > 0.5f - THR) {
       float e = __fdiv_rn(hi_of(v[j]), sk);
       if (has_z) e = __fadd_rn(e, zp);
       q1 = rhaz(e);
