@@ -33,6 +33,11 @@ W_NONZERO_THRESHOLD = 1e-8       # ldlq.py:505
 # Tensor-core passes of the lazy GPTQ/LDLQ update and the greedy cross terms:
 # 3 = 3xTF32 (~fp32 accurate, default), 1 = plain TF32 with fp32 accumulation.
 GEMM_PASSES = 3
+# Tensor-core passes of the greedy local search's cross terms E @ H[:, block]:
+# 3xTF32 by default (the codes follow the reference's fp32 search); 1 = plain
+# TF32 with fp32 accumulation, faster, with more near-ties broken the other
+# way (environment variable IC_GREEDY_GEMM_PASSES overrides).
+GREEDY_GEMM_PASSES = 3
 # Columns per super-block of the two-level lazy update (multiple of the block size).
 SUPERBLOCK = 1024
 

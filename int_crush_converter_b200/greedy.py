@@ -13,17 +13,28 @@ as the reference falls back to its v2 kernel.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _native as nat
 from ._dev import device_of, f32, split, workspace
-from .config import (EIGENVALUE_FLOOR, GEMM_PASSES, LOWRANK_MAX_K, LOWRANK_MAX_RANK_FRAC, LOWRANK_SKETCH,
+from .config import (EIGENVALUE_FLOOR, GREEDY_GEMM_PASSES, LOWRANK_MAX_K, LOWRANK_MAX_RANK_FRAC, LOWRANK_SKETCH,
                      STALL_THRESHOLD)
 
 
 def greedy_local_search(W: torch.Tensor, Q: torch.Tensor, scale_2d: torch.Tensor, H: torch.Tensor,
-                        num_passes: int, clamp_min: int, clamp_max: int) -> torch.Tensor:
-    """Returns int8 codes [M, N] minimising tr((Q*s - W) H (Q*s - W)^T) coordinate-wise."""
+                        num_passes: int, clamp_min: int, clamp_max: int, *,
+                        gemm_passes: int | None = None) -> torch.Tensor:
+    """Returns int8 codes [M, N] minimising tr((Q*s - W) H (Q*s - W)^T) coordinate-wise.
+    ``gemm_passes`` (1 or 3) sets the precision of the cross-term products;
+    default: the environment variable IC_GREEDY_GEMM_PASSES, else
+    ``config.GREEDY_GEMM_PASSES`` (3)."""
+    if gemm_passes is None:
+        gemm_passes = os.environ.get("IC_GREEDY_GEMM_PASSES") or GREEDY_GEMM_PASSES
+    gp = int(gemm_passes)
+    if gp not in (1, 3):
+        raise ValueError(f"gemm_passes must be 1 or 3, got {gemm_passes}")
     dev = device_of(W, Q, H)
     Wd = f32(W, dev)
     M, N = Wd.shape
@@ -35,7 +46,7 @@ def greedy_local_search(W: torch.Tensor, Q: torch.Tensor, scale_2d: torch.Tensor
     if M and N and num_passes > 0:
         nat.check(lib.ic_greedy_run(Wd.data_ptr(), N, Qd.data_ptr(), N, Sd.data_ptr(), N, hi.data_ptr(),
                                     lo.data_ptr(), hi.shape[1], M, N, int(num_passes), int(clamp_min),
-                                    int(clamp_max), GEMM_PASSES, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
+                                    int(clamp_max), gp, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
                   "greedy_run")
     out = Qd.clamp(clamp_min, clamp_max)
     return out if W.is_cuda else out.to(W.device)

@@ -180,12 +180,15 @@ def test_config2_rtn_int8_clip(M):
     assert codes_close(np_(out["codes"]), q)
 
 
-def test_config4_ldlq_rows_vs_oracle():
+@pytest.mark.parametrize("greedy_gemm_passes", ["3", "1"])
+def test_config4_ldlq_rows_vs_oracle(monkeypatch, greedy_gemm_passes):
     """LDLQ INT4 rot256, 2 iterations, 8 greedy passes, weight-only Hessian, one
     [8192, 8192] layer; the oracle runs 128 seeded rows with the full damped
     W^T W / M.  With 2 iterations the second pass's codes are the result
     whatever the convergence checks decide (ldlq.py:479-550), so rows stay
-    independent."""
+    independent.  Both precisions of the greedy cross terms (3xTF32, the
+    default, and the opt-in one-pass TF32)."""
+    monkeypatch.setenv("IC_GREEDY_GEMM_PASSES", greedy_gemm_passes)
     import warnings
     M = N = 8192
     W = gi.weight_outlier_cols(700, M, N, frac=0.0005, mult=30.0, std=0.015)

@@ -178,15 +178,19 @@ def test_piso_choices_cost_bound(golden, name):
     assert np.all(mine <= ref * (1 + 5e-5) + 1e-30), np.max(mine / ref - 1)
 
 
+@pytest.mark.parametrize("gemm_passes", [1, 3])
 @pytest.mark.parametrize("name", list(C.GREEDY_CASES))
-def test_greedy_rows_cost_bound(golden, name):
+def test_greedy_rows_cost_bound(golden, name, gemm_passes):
     """Per row, e H e^T of the greedy result within 1e-3 (relative) of the
     reference's: coordinate descent rows are independent, and rows whose codes
-    differ took a tie broken differently by fp32 rounding."""
+    differ took a near-tie broken differently by the rounding of the cross
+    terms.  With 3xTF32 cross terms (the default) over 99% of the codes are the
+    reference's; the opt-in one-pass TF32 products break more near-ties the
+    other way (98.8% on greedy4) and are held to the cost bound alone."""
     c = C.GREEDY_CASES[name]
     W, Q, S, H = C.greedy_inputs(c)
     qm = (-8, 7) if c["bits"] == 4 else (-128, 127)
-    out = np_(B.greedy_local_search(cu(W), cu(Q), cu(S), cu(H), c["passes"], *qm))
+    out = np_(B.greedy_local_search(cu(W), cu(Q), cu(S), cu(H), c["passes"], *qm, gemm_passes=gemm_passes))
     g = golden[name + "/codes"]
     Hd = H.astype(np.float64)
 
@@ -194,7 +198,8 @@ def test_greedy_rows_cost_bound(golden, name):
         E = q.astype(np.float64) * S - W
         return np.einsum("ij,ij->i", E @ Hd, E)
     assert np.all(rowcost(out) <= rowcost(g) * (1 + 1e-3) + 1e-30)
-    assert np.mean(out == g) > 0.99
+    if gemm_passes == 3:
+        assert np.mean(out == g) > 0.99
 
 
 @pytest.mark.parametrize("name", list(C.PQ_CASES))
