@@ -39,3 +39,20 @@ def test_binding_rejects_wrong_argument_count():
         lib.ic_rotate_hessian(None, 1, 4, 4, 4, None, None, 4, 4, None)  # one too many
     with pytest.raises(TypeError):
         lib.ic_version(1)
+
+
+def test_greedy_gemm_passes_validated_before_any_device_use(monkeypatch):
+    """The cross-term precision is 1 or 3 passes, from the keyword or the
+    IC_GREEDY_GEMM_PASSES environment variable; anything else is a ValueError
+    raised before a GPU is looked for."""
+    import pytest
+    import torch
+
+    from int_crush_converter_b200 import greedy
+    W = torch.zeros(2, 4)
+    Q = torch.zeros(2, 4)
+    with pytest.raises(ValueError, match="gemm_passes"):
+        greedy.greedy_local_search(W, Q, torch.ones(2, 4), torch.eye(4), 1, -8, 7, gemm_passes=2)
+    monkeypatch.setenv("IC_GREEDY_GEMM_PASSES", "5")
+    with pytest.raises(ValueError, match="gemm_passes"):
+        greedy.greedy_local_search(W, Q, torch.ones(2, 4), torch.eye(4), 1, -8, 7)
