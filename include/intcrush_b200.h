@@ -309,7 +309,10 @@ int ic_ldlq_update_scales(const float* W, const int8_t* Q, float* cur, const flo
  * coordinate descent over [qmin,qmax] minimising tr(E H E^T), E = Q*s - W.
  * Cross terms err * H[blk,:]^T per 128-column block on the tensor cores plus
  * exact in-block rank-1 corrections.  Q int8 [M,N] updated in place; H fp32
- * [N,N] as a hi/lo pair (ldh % 4 == 0). */
+ * [N,N] as a hi/lo pair (ldh % 4 == 0).  gemm_passes: 3 = cross terms in
+ * 3xTF32, 1 = one TF32 pass with fp32 accumulation (the products read h_hi
+ * alone, the in-block terms still the exact pair; more near-ties broken the
+ * other way). */
 size_t ic_greedy_workspace_size(int64_t M, int64_t N);
 int ic_greedy_run(const float* W, int64_t ldw, int8_t* Q, int64_t ldq, const float* scale2d,
                   int64_t lds, const float* h_hi, const float* h_lo, int64_t ldh, int64_t M,
